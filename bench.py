@@ -1,0 +1,425 @@
+"""Benchmark of the remora_b200 hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload gemm|elementwise]
+
+Default workload (the headline config): stablehlo.dot_general GEMM, bf16
+A [8192,8192] x B [8192,8192] -> bf16, fp32 accumulate, U(-1,1) seeded
+inputs.  Under torchrun with N > 1 GPUs the workload is the batched form
+[8,4096,4096] x [8,4096,4096] with the batch split across ranks (no
+collective; the same 1.0995e12 FLOP per step in total, strong scaling).
+One step = one GEMM over the whole job's batch.  Rank 0 prints one JSON line.
+
+--impl reference times the reference's CPU path for the same metric: the C
+restatement of remora's convert-linalg-to-loops loop nest (oracle/), on all
+host threads, over a bounded row sample of the same GEMM per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE layer tokens/s; GEMM/attn TFLOP/s as % B200 peak; elementwise HBM GB/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant
+# kernel, from the ncu captures summarised in profiles/ (None = not captured).
+NCU_TRAFFIC_BYTES = {
+    "gemm_8192": None,
+    "gemm_batched": None,
+    "elementwise": None,
+}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+               0x2: "applications_clocks_setting"}
+
+    def __init__(self, device_index: int, period_s: float = 0.02):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self.period = period_s
+        self._stop = threading.Event()
+        self._thread = None
+        self.ok = False
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            if not uuid.startswith("GPU-"):
+                uuid = "GPU-" + uuid
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # reading clocks is best effort; report it
+            self.err = repr(e)
+
+    def _run(self):
+        nv = self.nv
+        get_r = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = get_r(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *a):
+        if self._thread:
+            self._stop.set()
+            self._thread.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [],
+                    "note": "NVML unavailable: " + getattr(self, "err", "")}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------- distributed
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        if args.impl == "ours":
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ------------------------------------------------------------- CPU timing
+_CPU_INPUTS: dict = {}
+
+
+def cpu_gemm_rows_rate(rows_per_call: int, budget_s: float, threads: int):
+    """Times the oracle's bf16 GEMM loop nest on rows of the 8192^3 problem.
+
+    Returns (TFLOP/s, rows timed, seconds).  The rows are the first rows of
+    the same seeded A, the full seeded B.
+    """
+    import oracle
+
+    oracle.set_threads(threads)
+    K = N = 8192
+    key = ("gemm", rows_per_call)
+    if key not in _CPU_INPUTS:
+        _CPU_INPUTS.clear()
+        b = oracle.to_bf16(oracle.uniform("gemm_b", (K, N)))
+        a_rows = oracle.to_bf16(oracle.uniform("gemm_a", (rows_per_call * 4, K)))
+        _CPU_INPUTS[key] = (a_rows, b)
+    a_rows, b = _CPU_INPUTS[key]
+    done, t0 = 0, time.perf_counter()
+    while True:
+        r0 = (done % (rows_per_call * 4))
+        oracle.gemm_bf16_rows(a_rows, b, r0, r0 + rows_per_call)
+        done += rows_per_call
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    return 2.0 * done * N * K / el / 1e12, done, el
+
+
+def cpu_baseline_gemm(budget_s: float = 12.0):
+    import oracle
+
+    threads = os.cpu_count() or 1
+    rate, rows, el = cpu_gemm_rows_rate(max(threads, 1), budget_s, threads)
+    return {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{rows} output rows of the 8192^3 bf16 GEMM (oracle/oracle.c "
+                      f"orc_gemm_bf16_rows, gcc -O2 -fopenmp, {threads} threads), {el:.1f} s"}
+
+
+# -------------------------------------------------------------------- GEMM
+def bench_gemm(args, world, rank, local):
+    import torch
+
+    import remora_b200 as rb
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world == 1:
+        batch_local, M, N, K = 1, 8192, 8192, 8192
+        workload = "dot_general bf16 [8192,8192]x[8192,8192]->[8192,8192], fp32 accumulate"
+        cfg_key = "gemm_8192"
+    else:
+        if 8 % world:
+            raise SystemExit("batched GEMM shards a batch of 8: --gpus must divide 8")
+        batch_local, M, N, K = 8 // world, 4096, 4096, 4096
+        workload = (f"dot_general bf16 batched [8,4096,4096]x[8,4096,4096], batch sharded "
+                    f"{batch_local} per rank over {world} GPUs")
+        cfg_key = "gemm_batched"
+    flop_step = 2.0 * 8192 ** 3  # the whole job's work per step (both forms)
+    A = torch.empty(batch_local, M, K, dtype=torch.bfloat16, device=dev)
+    B = torch.empty(batch_local, K, N, dtype=torch.bfloat16, device=dev)
+    C = torch.empty(batch_local, M, N, dtype=torch.bfloat16, device=dev)
+    # each rank fills its own batch slice of the job's seeded tensors
+    rb.fill_uniform(A, rb.stream_key(10 + 100 * rank))
+    rb.fill_uniform(B, rb.stream_key(11 + 100 * rank))
+    a2, b2, c2 = (A[0], B[0], C[0]) if batch_local == 1 else (A, B, C)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        rb.gemm(a2, b2, out=c2)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    ms = max_over_ranks(ms_local, world)
+    value = flop_step / (ms * 1e-3) / 1e12
+
+    # end to end through the public API: pinned host inputs in, result out
+    Ah = torch.empty(A.shape, dtype=A.dtype, pin_memory=True)
+    Bh = torch.empty(B.shape, dtype=B.dtype, pin_memory=True)
+    Ch = torch.empty(C.shape, dtype=C.dtype, pin_memory=True)
+    Ah.copy_(A)
+    Bh.copy_(B)
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        A.copy_(Ah, non_blocking=True)
+        B.copy_(Bh, non_blocking=True)
+        rb.gemm(a2, b2, out=c2)
+        Ch.copy_(C, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ev0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / e2e_steps, world)
+    h2d = (A.numel() + B.numel()) * 2 * world
+    d2h = C.numel() * 2 * world
+
+    peaks, src = load_peaks()
+    achieved = 2.0 * batch_local * M * N * K / (ms_local * 1e-3) / 1e12
+    traffic = NCU_TRAFFIC_BYTES.get(cfg_key)
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded U(-1,1) bf16)",
+        "config": {"workload": workload, "M": M, "N": N, "K": K, "batch": 8 if world > 1 else 1,
+                   "parallelism": f"batch-sharded x{world}" if world > 1 else "single GPU",
+                   "l2": f"inputs {(A.numel() + B.numel()) * 2 / 2**20:.0f} MiB per GPU "
+                         "> 126 MB L2 (no flush)"},
+        "roofline": {"bound": "tensor", "achieved": achieved,
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"],
+                     "peak_sustained": peaks.get("bf16_tflops_sustained"),
+                     "peak_source": src, "traffic": traffic,
+                     "kernel": "rb::gemm::k_gemm_bf16<true>"},
+        "e2e": {"value": flop_step / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+    return line
+
+
+# ------------------------------------------------------------- elementwise
+def bench_elementwise(args, world, rank, local):
+    """scale -> add -> exp chain: the named [1,8,128,128] shape (latency
+    bound, L2 resident) and a 2^28-element sweep where HBM BW is judged."""
+    import torch
+
+    import remora_b200 as rb
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    n = 1 << 28
+    s = torch.empty(n, device=dev)
+    b = torch.empty(n, device=dev)
+    o = torch.empty(n, device=dev)
+    rb.fill_normal(s, rb.stream_key(1))
+    rb.fill_normal(b, rb.stream_key(2))
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(args.warmup):
+        rb.scale_add_exp(s, b, 0.125, out=o)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            rb.scale_add_exp(s, b, 0.125, out=o)
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    bytes_step = 12.0 * n * world
+    gbs = bytes_step / (ms * 1e-3) / 1e9
+    small = rb.run_test("elementwise_chain", device=local, iters=200, warmup=20)
+    peaks, src = load_peaks()
+    return {
+        "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) f32)",
+        "config": {"workload": "exp(s*0.125+b) f32, 2^28 elements (3 GiB per step)",
+                   "named_shape_us_per_call": small["ms_per_iter"] * 1e3,
+                   "l2": "inputs 2 GiB > 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": gbs / world / peaks["hbm_gbs"],
+                     "peak_source": src, "traffic": NCU_TRAFFIC_BYTES.get("elementwise")},
+        "gpu_launches": args.steps, "clocks": clk.summary(),
+    }
+
+
+# --------------------------------------------------------- reference arm
+def reference_arm(args, world, rank):
+    """The reference's CPU path (its loop nest, restated in oracle/) on all
+    host threads, on a bounded row sample of the same GEMM per step."""
+    if rank != 0:
+        return None
+    import oracle
+
+    threads = os.cpu_count() or 1
+    # calibrate: rows per step so that the whole run stays within ~2 minutes
+    rate, rows, el = cpu_gemm_rows_rate(threads, 2.0, threads)
+    sec_per_row = el / rows
+    per_step = max(1, int(min(threads * 4, 100.0 / (args.steps + args.warmup) / sec_per_row)))
+    for _ in range(args.warmup):
+        cpu_gemm_rows_rate(per_step, 0.0, threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_gemm_rows_rate(per_step, 0.0, threads)
+    el = time.perf_counter() - t0
+    v = 2.0 * per_step * 8192 * 8192 * args.steps / el / 1e12
+    sample = (f"{per_step} output rows of the 8192^3 bf16 GEMM per step "
+              f"(oracle/oracle.c loop nest, {threads} threads)")
+    return {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded U(-1,1) bf16)",
+        "config": {"workload": "dot_general bf16 [8192,8192]x[8192,8192]->[8192,8192], fp32 "
+                               "accumulate (row sample per step)"},
+        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["gemm", "elementwise"], default="gemm")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        line = reference_arm(args, world, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+    from remora_b200 import build
+
+    build.build()  # no-op when the in-tree library is current
+    fn = {"gemm": bench_gemm, "elementwise": bench_elementwise}[args.workload]
+    line = fn(args, world, rank, local)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_gemm() if args.workload == "gemm" else None
+    elif rank == 0:
+        line["cpu_baseline"] = None
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

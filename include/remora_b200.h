@@ -1,0 +1,154 @@
+/*
+ * remora_b200.h -- C ABI of the B200 (sm_100a) execution backend for remora.
+ *
+ * remora's GPU harness, `int launchOnGpu(const std::vector<std::string>&
+ * ptxModules, llvm::StringRef test)` (compiler/gpu_tests.h:6-9,
+ * compiler/gpu_tests.cpp:101-125), loads NVVM-generated sm_89 PTX and
+ * launches it with the MLIR memref-descriptor argument list
+ * (compiler/gpu_tests.cpp:58-79).  This library replaces what sits below
+ * that call for the programs it recognises: `launchOnGpu` asks
+ * remora_b200_recognise(test) and, if recognised, calls
+ * remora_b200_run_test() instead of loading the PTX.  The per-op entry
+ * points take caller-owned device pointers, plain sizes and a CUDA stream.
+ *
+ * Conventions
+ *   - Every function returns an int status: REMORA_B200_OK (0) or a negative
+ *     REMORA_B200_ERR_* code; remora_b200_last_error() gives the text
+ *     (thread-local).  remora's CUDA_CHECK returned 1 on any failure
+ *     (gpu_tests.cpp:11-20); a caller that wants that convention maps
+ *     "status != 0" to 1.  A failed parity check IS an error here, unlike
+ *     gpu_tests.cpp:91-94.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream).  Launches are stream-ordered and asynchronous unless stated.
+ *   - bf16 tensors are passed as void* to 16-bit storage.  Row-major unless
+ *     stated.  Leading dimensions are in elements.
+ *   - The per-op entry points never allocate or free caller memory.
+ */
+#ifndef REMORA_B200_H
+#define REMORA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define REMORA_B200_OK 0
+#define REMORA_B200_ERR_INVALID (-1)     /* bad argument, shape or alignment */
+#define REMORA_B200_ERR_CUDA (-2)        /* CUDA runtime / driver error */
+#define REMORA_B200_ERR_NCCL (-3)        /* NCCL error */
+#define REMORA_B200_ERR_TIMEOUT (-4)     /* a bounded device or host wait expired */
+#define REMORA_B200_ERR_PARITY (-5)      /* run_test: results outside tolerance */
+#define REMORA_B200_ERR_UNSUPPORTED (-6) /* test kind not recognised */
+
+/* B operand layouts of the GEMM entry points. */
+#define REMORA_B200_B_KN 0 /* B is [K, N], N contiguous (dot_general rhs [K,N]) */
+#define REMORA_B200_B_NK 1 /* B is [N, K], K contiguous (transposed rhs)        */
+
+/* Text of the last error raised on the calling thread ("" if none). */
+const char* remora_b200_last_error(void);
+
+/* Library version, major*10000 + minor*100 + patch. */
+int remora_b200_version(void);
+
+/* ------------------------------------------------------------------------
+ * Dispatcher (replaces the body of launchOnGpu, gpu_tests.cpp:101-125)
+ * --------------------------------------------------------------------- */
+
+/* Options of one run_test call.  Zero-initialise, then set what you need. */
+typedef struct remora_b200_opts {
+  int device;       /* CUDA device ordinal (remora uses device 0, gpu_tests.cpp:103) */
+  uint64_t seed;    /* base seed of the input generator; 0 means 42 */
+  int iters;        /* timed iterations (0 = 1) */
+  int warmup;       /* untimed warm-up iterations */
+  int validate;     /* 1 = check the result (known answer or sampled self-check) */
+  const char* config; /* optional named configuration, NULL = the reference program's shape */
+} remora_b200_opts;
+
+typedef struct remora_b200_report {
+  double ms_per_iter;   /* CUDA-event time per iteration */
+  double work;          /* algorithmic FLOPs or bytes per iteration */
+  double rate;          /* work / time, in FLOP/s or B/s */
+  double max_abs_err;   /* validation: worst absolute error */
+  double max_rel_err;   /* validation: worst relative error */
+  int64_t checked;      /* number of output elements checked */
+  int passed;           /* 1 if validation passed (or was not requested) */
+  char detail[256];     /* one-line human readable summary */
+} remora_b200_report;
+
+/* 1 if `test` (the --test= kind) is handled by this library, else 0.
+ * Kinds: "elementwise" (gpu_tests.cpp:35-95), "projection"
+ * (cpu_tests.cpp:65-97), "elementwise_chain", "gemm". */
+int remora_b200_recognise(const char* test);
+
+/* Runs the recognised program end to end on `o->device`: allocates its own
+ * buffers, fills the inputs, launches, times and validates.  Replaces
+ * launchElementwiseOnGpu (gpu_tests.cpp:35-95), which allocated, filled
+ * x = 1 and bias = -0.5, launched and checked |v - 0.5| <= 1e-5. */
+int remora_b200_run_test(const char* test, const remora_b200_opts* o, remora_b200_report* r);
+
+/* ------------------------------------------------------------------------
+ * Elementwise attention epilogue
+ * --------------------------------------------------------------------- */
+
+/* out[r, j] = maximumf(x[r, j] + bias[j], 0) for r < rows, j < d.
+ * The fused linalg.generic of
+ * mlir/linalg/attention_elementwise_lowered_to_linalg.mlir:7-11 (the
+ * --test=elementwise program, mlir/stablehlo/simple_attention_elementwise.mlir:5-17).
+ * NaN propagates; -0 becomes +0. */
+int remora_b200_relu_bias_f32(const float* x, const float* bias, float* out, int64_t rows,
+                              int64_t d, void* stream);
+
+/* out[i] = exp(s[i] * scale + b[i]) for i < n: stablehlo.multiply by a
+ * scalar, stablehlo.add, stablehlo.exponential, one HBM round trip.  The
+ * product and the sum are rounded separately (no contraction). */
+int remora_b200_scale_add_exp_f32(const float* s, const float* b, float* out, int64_t n,
+                                  float scale, void* stream);
+
+/* ------------------------------------------------------------------------
+ * stablehlo.dot_general GEMM (contracting lhs dim 1 x rhs dim 0)
+ * --------------------------------------------------------------------- */
+
+/* C[b] = A[b] * B[b] for b < batch: bf16 inputs, fp32 accumulation in
+ * tensor memory, bf16 output (round to nearest even).
+ * A: [M, K] (lda), B: [K, N] (ldb) if b_layout == REMORA_B200_B_KN else
+ * [N, K], C: [M, N] (ldc).  stride_a/b/c: elements between batches.
+ * Requires K % 8 == 0, N % 8 == 0, lda/ldb/ldc % 8 == 0 and 16-byte
+ * aligned base pointers (TMA rules); M, N, K need not be tile multiples.
+ * Replaces the two NVVM modules (fill + reduction) that remora emits for
+ * mlir/linalg/attention_projection_lowered_to_linalg.mlir:8-12
+ * (compiler/gpu.cpp:159-160), which gpu_tests.cpp:119 never launches. */
+int remora_b200_gemm_bf16(const void* A, const void* B, void* C, int64_t batch, int64_t M,
+                          int64_t N, int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                          int64_t stride_a, int64_t stride_b, int64_t stride_c, int b_layout,
+                          void* stream);
+
+/* f32 dot_general with the reference CPU path's exact arithmetic: for each
+ * output, fill 0 then out = out + a*b over k in increasing order, each
+ * product and sum rounded separately (cpu.cpp:50-55 convert-linalg-to-loops
+ * of attention_projection_lowered_to_linalg.mlir:8-12).  Results are
+ * bit-identical to that loop nest.  The --test=projection program. */
+int remora_b200_gemm_f32_exact(const float* A, const float* B, float* C, int64_t M, int64_t N,
+                               int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int b_layout,
+                               void* stream);
+
+/* ------------------------------------------------------------------------
+ * Seeded input generator (device side of the counter-based generator the
+ * tests and benchmarks use; one stream key per tensor)
+ * --------------------------------------------------------------------- */
+
+/* out[i] = mean + sigma * N(0,1) draw i (Box-Muller in double), as f32
+ * (dtype 0) or bf16 (dtype 1, f32 then round to nearest even). */
+int remora_b200_fill_normal(void* out, int64_t n, int dtype, uint64_t key, double mean,
+                            double sigma, void* stream);
+
+/* out[i] = lo + (hi - lo) * U(0,1) draw i, as f32 (dtype 0) or bf16 (1). */
+int remora_b200_fill_uniform(void* out, int64_t n, int dtype, uint64_t key, double lo,
+                             double hi, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* REMORA_B200_H */

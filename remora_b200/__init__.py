@@ -1,0 +1,238 @@
+"""remora_b200 -- B200 (sm_100a) execution backend for remora's recognised
+data-parallel programs.
+
+The product is ``libremora_b200.so`` (CUDA kernels + the C ABI declared in
+``include/remora_b200.h``).  This module is the host-side mirror of that ABI
+for Python callers: it loads the library with ctypes and passes torch CUDA
+tensors as raw device pointers on the current CUDA stream.  There is no CPU
+path: if the library is missing, or a tensor is not on a CUDA device, the
+call raises.
+
+remora's own harness entry point is ``launchOnGpu(ptxModules, test)``
+(compiler/gpu_tests.h:6-9); ``recognise`` / ``run_test`` mirror the
+dispatcher that replaces its body.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libremora_b200.so")
+_lib = None
+
+OK = 0
+ERR_INVALID = -1
+ERR_CUDA = -2
+ERR_NCCL = -3
+ERR_TIMEOUT = -4
+ERR_PARITY = -5
+ERR_UNSUPPORTED = -6
+
+B_KN = 0
+B_NK = 1
+
+
+class RemoraError(RuntimeError):
+    """A non-zero status from the C ABI, with remora_b200_last_error() text."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"remora_b200 error {code}: {msg}")
+        self.code = code
+
+
+class Opts(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("seed", ctypes.c_uint64), ("iters", ctypes.c_int),
+                ("warmup", ctypes.c_int), ("validate", ctypes.c_int), ("config", ctypes.c_char_p)]
+
+
+class Report(ctypes.Structure):
+    _fields_ = [("ms_per_iter", ctypes.c_double), ("work", ctypes.c_double),
+                ("rate", ctypes.c_double), ("max_abs_err", ctypes.c_double),
+                ("max_rel_err", ctypes.c_double), ("checked", ctypes.c_int64),
+                ("passed", ctypes.c_int), ("detail", ctypes.c_char * 256)]
+
+
+P, I64, I, F, D, U64 = (ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_float,
+                        ctypes.c_double, ctypes.c_uint64)
+
+_SIGNATURES = {
+    "remora_b200_last_error": ([], ctypes.c_char_p),
+    "remora_b200_version": ([], I),
+    "remora_b200_recognise": ([ctypes.c_char_p], I),
+    "remora_b200_run_test": ([ctypes.c_char_p, ctypes.POINTER(Opts), ctypes.POINTER(Report)], I),
+    "remora_b200_relu_bias_f32": ([P, P, P, I64, I64, P], I),
+    "remora_b200_scale_add_exp_f32": ([P, P, P, I64, F, P], I),
+    "remora_b200_gemm_bf16": ([P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I, P], I),
+    "remora_b200_gemm_f32_exact": ([P, P, P, I64, I64, I64, I64, I64, I64, I, P], I),
+    "remora_b200_fill_normal": ([P, I64, I, U64, D, D, P], I),
+    "remora_b200_fill_uniform": ([P, I64, I, U64, D, D, P], I),
+}
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded C ABI.  Raises if libremora_b200.so has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -m remora_b200.build` "
+                "(remora_b200 has no CPU fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (args, res) in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    return lib().remora_b200_last_error().decode()
+
+
+def _check(rc: int) -> None:
+    if rc != OK:
+        raise RemoraError(rc, last_error())
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _dev(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("remora_b200 operates on CUDA tensors only (no CPU fallback)")
+
+
+def _bf16(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t.dtype != torch.bfloat16:
+            raise TypeError(f"expected a bfloat16 tensor, got {t.dtype}")
+
+
+# --------------------------------------------------------------- dispatcher
+def recognise(test: str) -> bool:
+    return bool(lib().remora_b200_recognise(test.encode()))
+
+
+def run_test(test: str, device: int = 0, seed: int = 42, iters: int = 1, warmup: int = 0,
+             validate: bool = True, config: str | None = None) -> dict:
+    """Runs a recognised --test=<kind> program end to end; raises on failure."""
+    o = Opts(device, seed, iters, warmup, int(validate), config.encode() if config else None)
+    r = Report()
+    rc = lib().remora_b200_run_test(test.encode(), ctypes.byref(o), ctypes.byref(r))
+    rep = {k: getattr(r, k) for k, _ in Report._fields_ if k != "detail"}
+    rep["detail"] = r.detail.decode()
+    if rc != OK:
+        raise RemoraError(rc, last_error())
+    return rep
+
+
+# -------------------------------------------------------------- elementwise
+def relu_bias(x: torch.Tensor, bias: torch.Tensor, out: torch.Tensor | None = None):
+    """maximumf(x + bias, 0), bias broadcast over the last dim (f32)."""
+    _dev(x, bias)
+    if x.dtype != torch.float32 or bias.dtype != torch.float32:
+        raise TypeError("relu_bias takes float32 tensors")
+    if bias.dim() != 1 or x.shape[-1] != bias.shape[0]:
+        raise ValueError("bias must be 1-D and match x's last dim")
+    x = x.contiguous()
+    out = torch.empty_like(x) if out is None else out
+    d = bias.shape[0]
+    _check(lib().remora_b200_relu_bias_f32(x.data_ptr(), bias.contiguous().data_ptr(),
+                                           out.data_ptr(), x.numel() // d, d, _stream(x)))
+    return out
+
+
+def scale_add_exp(s: torch.Tensor, b: torch.Tensor, scale: float,
+                  out: torch.Tensor | None = None):
+    """exp(s * scale + b), f32, elementwise."""
+    _dev(s, b)
+    if s.shape != b.shape or s.dtype != torch.float32 or b.dtype != torch.float32:
+        raise ValueError("scale_add_exp takes two float32 tensors of one shape")
+    s, b = s.contiguous(), b.contiguous()
+    out = torch.empty_like(s) if out is None else out
+    _check(lib().remora_b200_scale_add_exp_f32(s.data_ptr(), b.data_ptr(), out.data_ptr(),
+                                               s.numel(), float(scale), _stream(s)))
+    return out
+
+
+# --------------------------------------------------------------------- GEMM
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+         b_layout: int = B_KN) -> torch.Tensor:
+    """dot_general: a [.., M, K] x b [.., K, N] (or [.., N, K] with B_NK), bf16."""
+    _dev(a, b)
+    _bf16(a, b)
+    batched = a.dim() == 3
+    a3 = a if batched else a.unsqueeze(0)
+    b3 = b if b.dim() == 3 else b.unsqueeze(0)
+    if a3.stride(-1) != 1 or b3.stride(-1) != 1:
+        raise ValueError("gemm operands must have a unit innermost stride")
+    batch, M, K = a3.shape
+    if b3.shape[0] != batch:
+        raise ValueError("batch mismatch")
+    if b_layout == B_KN:
+        Kb, N = b3.shape[1], b3.shape[2]
+    else:
+        N, Kb = b3.shape[1], b3.shape[2]
+    if Kb != K:
+        raise ValueError(f"contracting dims differ: {K} vs {Kb}")
+    if out is None:
+        out = torch.empty((batch, M, N) if batched else (M, N), dtype=torch.bfloat16,
+                          device=a.device)
+    c3 = out if out.dim() == 3 else out.unsqueeze(0)
+    _check(lib().remora_b200_gemm_bf16(
+        a3.data_ptr(), b3.data_ptr(), c3.data_ptr(), batch, M, N, K, a3.stride(1), b3.stride(1),
+        c3.stride(1), a3.stride(0), b3.stride(0), c3.stride(0), b_layout, _stream(a)))
+    return out
+
+
+def gemm_f32_exact(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+                   b_layout: int = B_KN) -> torch.Tensor:
+    """f32 dot_general with the reference loop nest's exact rounding sequence."""
+    _dev(a, b)
+    if a.dtype != torch.float32 or b.dtype != torch.float32:
+        raise TypeError("gemm_f32_exact takes float32 tensors")
+    M, K = a.shape
+    N = b.shape[1] if b_layout == B_KN else b.shape[0]
+    a, b = a.contiguous(), b.contiguous()
+    out = torch.empty((M, N), dtype=torch.float32, device=a.device) if out is None else out
+    _check(lib().remora_b200_gemm_f32_exact(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K,
+                                            a.stride(0), b.stride(0), out.stride(0), b_layout,
+                                            _stream(a)))
+    return out
+
+
+# ---------------------------------------------------------- seeded inputs
+def fill_normal(t: torch.Tensor, key: int, mean: float = 0.0, sigma: float = 1.0):
+    _dev(t)
+    dt = {torch.float32: 0, torch.bfloat16: 1}[t.dtype]
+    _check(lib().remora_b200_fill_normal(t.data_ptr(), t.numel(), dt, key, mean, sigma,
+                                         _stream(t)))
+    return t
+
+
+def fill_uniform(t: torch.Tensor, key: int, lo: float = -1.0, hi: float = 1.0):
+    _dev(t)
+    dt = {torch.float32: 0, torch.bfloat16: 1}[t.dtype]
+    _check(lib().remora_b200_fill_uniform(t.data_ptr(), t.numel(), dt, key, lo, hi, _stream(t)))
+    return t
+
+
+_G = 0x9E3779B97F4A7C15
+_MASK = (1 << 64) - 1
+
+
+def _mix64(z: int) -> int:
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _MASK
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _MASK
+    return z ^ (z >> 31)
+
+
+def stream_key(stream: int, seed: int = 42) -> int:
+    """Key of tensor stream `stream` under base seed `seed` (generator key schedule)."""
+    return _mix64((seed * _G + stream) & _MASK)

@@ -1,0 +1,284 @@
+// dispatch.cu -- the --test=<kind> dispatcher that replaces the body of
+// remora's launchOnGpu (compiler/gpu_tests.cpp:101-125) for recognised
+// programs.  Each kind owns its buffers end to end, fills its inputs,
+// launches through the per-op C ABI, times with CUDA events and validates on
+// the host, as launchElementwiseOnGpu (gpu_tests.cpp:35-95) did -- except
+// that a validation failure is a non-zero status here.
+#include <cmath>
+#include <string>
+#include <vector>
+
+#include "runtime.cuh"
+
+namespace rb {
+
+struct DevBuf {
+  void* p = nullptr;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+  int alloc(size_t bytes) {
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess)
+      return fail(REMORA_B200_ERR_CUDA, "cudaMalloc(%zu): %s", bytes, cudaGetErrorString(e));
+    return REMORA_B200_OK;
+  }
+};
+
+struct Timer {
+  cudaEvent_t a = nullptr, b = nullptr;
+  ~Timer() {
+    if (a) cudaEventDestroy(a);
+    if (b) cudaEventDestroy(b);
+  }
+};
+
+static uint64_t host_mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Stream key of tensor `stream` under `seed` (the generator's key schedule).
+static uint64_t stream_key(uint64_t seed, uint64_t stream) {
+  return host_mix64(seed * 0x9E3779B97F4A7C15ull + stream);
+}
+
+static float bf16_to_f32(uint16_t h) {
+  uint32_t u = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+// Relative error as |g - r| / max(|r|, floor), floor = 1e-3 * max|r|.
+struct ErrStat {
+  double max_abs = 0, max_rel = 0;
+  int64_t n = 0;
+  void add(double g, double r, double floor) {
+    double a = std::fabs(g - r);
+    double d = std::max(std::fabs(r), floor);
+    if (!(a <= max_abs)) max_abs = a;
+    double rel = d > 0 ? a / d : a;
+    if (!(rel <= max_rel)) max_rel = rel;
+    ++n;
+  }
+};
+
+template <class F>
+static int time_iters(const remora_b200_opts* o, cudaStream_t st, F&& launch, double* ms) {
+  Timer t;
+  RB_CUDA(cudaEventCreate(&t.a));
+  RB_CUDA(cudaEventCreate(&t.b));
+  int iters = o && o->iters > 0 ? o->iters : 1;
+  int warm = o ? o->warmup : 0;
+  for (int i = 0; i < warm; ++i) {
+    int rc = launch();
+    if (rc) return rc;
+  }
+  RB_CUDA(cudaEventRecord(t.a, st));
+  for (int i = 0; i < iters; ++i) {
+    int rc = launch();
+    if (rc) return rc;
+  }
+  RB_CUDA(cudaEventRecord(t.b, st));
+  RB_CUDA(cudaEventSynchronize(t.b));
+  float f = 0;
+  RB_CUDA(cudaEventElapsedTime(&f, t.a, t.b));
+  *ms = (double)f / iters;
+  return collect_device_error(st);
+}
+
+static void finish(remora_b200_report* r, double ms, double work, const ErrStat& e, double tol,
+                   bool validate, const char* what, const char* unit) {
+  r->ms_per_iter = ms;
+  r->work = work;
+  r->rate = ms > 0 ? work / (ms * 1e-3) : 0;
+  r->max_abs_err = e.max_abs;
+  r->max_rel_err = e.max_rel;
+  r->checked = e.n;
+  r->passed = !validate || (e.n > 0 && e.max_rel <= tol);
+  snprintf(r->detail, sizeof(r->detail), "%s: %.4f ms/iter, %.3f %s, checked %lld, max rel %.3g (tol %.1g) %s",
+           what, ms, r->rate * 1e-12, unit, (long long)e.n, e.max_rel, tol,
+           validate ? (r->passed ? "PASS" : "FAIL") : "");
+}
+
+// --test=elementwise: relu(x + bias) on f32 [1,512,768], x = 1, bias = -0.5,
+// expected 0.5 everywhere within 1e-5 (gpu_tests.cpp:36, :53-56, :88-91).
+static int run_elementwise(const remora_b200_opts* o, remora_b200_report* r, cudaStream_t st) {
+  const int64_t N = 1, T = 512, D = 768, n = N * T * D;
+  DevBuf x, b, out;
+  int rc;
+  if ((rc = x.alloc(n * 4)) || (rc = b.alloc(D * 4)) || (rc = out.alloc(n * 4))) return rc;
+  std::vector<float> hx(n, 1.0f), hb(D, -0.5f), ho(n);
+  RB_CUDA(cudaMemcpyAsync(x.p, hx.data(), n * 4, cudaMemcpyHostToDevice, st));
+  RB_CUDA(cudaMemcpyAsync(b.p, hb.data(), D * 4, cudaMemcpyHostToDevice, st));
+  double ms = 0;
+  rc = time_iters(o, st, [&] {
+    return remora_b200_relu_bias_f32((const float*)x.p, (const float*)b.p, (float*)out.p, N * T,
+                                     D, st);
+  }, &ms);
+  if (rc) return rc;
+  RB_CUDA(cudaMemcpy(ho.data(), out.p, n * 4, cudaMemcpyDeviceToHost));
+  ErrStat e;
+  for (float v : ho) e.add(v, 0.5, 0.0);
+  finish(r, ms, (double)(2 * n * 4 + D * 4), e, 1e-5 / 0.5, true, "elementwise relu(x+bias)",
+         "TB/s");
+  return REMORA_B200_OK;
+}
+
+// --test=projection: x = 1 [1,512,768] . w = 1/768 [768,768] -> 1.0
+// (cpu_tests.cpp:65-97), through the exact f32 path.
+static int run_projection(const remora_b200_opts* o, remora_b200_report* r, cudaStream_t st) {
+  const int64_t M = 512, K = 768, N = 768;
+  DevBuf x, w, out;
+  int rc;
+  if ((rc = x.alloc(M * K * 4)) || (rc = w.alloc(K * N * 4)) || (rc = out.alloc(M * N * 4)))
+    return rc;
+  std::vector<float> hx(M * K, 1.0f), hw(K * N, 1.0f / 768.0f), ho(M * N);
+  RB_CUDA(cudaMemcpyAsync(x.p, hx.data(), hx.size() * 4, cudaMemcpyHostToDevice, st));
+  RB_CUDA(cudaMemcpyAsync(w.p, hw.data(), hw.size() * 4, cudaMemcpyHostToDevice, st));
+  double ms = 0;
+  rc = time_iters(o, st, [&] {
+    return remora_b200_gemm_f32_exact((const float*)x.p, (const float*)w.p, (float*)out.p, M, N,
+                                      K, K, N, N, REMORA_B200_B_KN, st);
+  }, &ms);
+  if (rc) return rc;
+  RB_CUDA(cudaMemcpy(ho.data(), out.p, ho.size() * 4, cudaMemcpyDeviceToHost));
+  // The loop nest's own value: fill 0, then 768 separately rounded adds.
+  float expect = 0.0f;
+  {
+    volatile float a = 0.0f;
+    for (int k = 0; k < 768; ++k) {
+      volatile float p = 1.0f * (1.0f / 768.0f);
+      a = a + p;
+    }
+    expect = a;
+  }
+  ErrStat e;
+  for (float v : ho) e.add(v, expect, 0.0);
+  finish(r, ms, 2.0 * M * N * K, e, 1e-5, true, "projection f32 exact", "TFLOP/s");
+  return REMORA_B200_OK;
+}
+
+// The scale -> add -> exp chain on f32 [1,8,128,128] seeded N(0,1).
+static int run_chain(const remora_b200_opts* o, remora_b200_report* r, cudaStream_t st) {
+  const int64_t n = 1 * 8 * 128 * 128;
+  const uint64_t seed = o && o->seed ? o->seed : 42;
+  DevBuf s, b, out;
+  int rc;
+  if ((rc = s.alloc(n * 4)) || (rc = b.alloc(n * 4)) || (rc = out.alloc(n * 4))) return rc;
+  if ((rc = remora_b200_fill_normal(s.p, n, 0, stream_key(seed, 1), 0.0, 1.0, st))) return rc;
+  if ((rc = remora_b200_fill_normal(b.p, n, 0, stream_key(seed, 2), 0.0, 1.0, st))) return rc;
+  const float scale = 0.125f;  // 1/sqrt(64)
+  double ms = 0;
+  rc = time_iters(o, st, [&] {
+    return remora_b200_scale_add_exp_f32((const float*)s.p, (const float*)b.p, (float*)out.p, n,
+                                         scale, st);
+  }, &ms);
+  if (rc) return rc;
+  std::vector<float> hs(n), hb(n), ho(n);
+  RB_CUDA(cudaMemcpy(hs.data(), s.p, n * 4, cudaMemcpyDeviceToHost));
+  RB_CUDA(cudaMemcpy(hb.data(), b.p, n * 4, cudaMemcpyDeviceToHost));
+  RB_CUDA(cudaMemcpy(ho.data(), out.p, n * 4, cudaMemcpyDeviceToHost));
+  ErrStat e;
+  for (int64_t i = 0; i < n; ++i) {
+    volatile float t = hs[i] * scale;
+    volatile float u = t + hb[i];
+    e.add(ho[i], (double)expf(u), 0.0);
+  }
+  finish(r, ms, (double)n * 12, e, 1e-5, o ? o->validate : 0, "scale-add-exp chain", "TB/s");
+  return REMORA_B200_OK;
+}
+
+// dot_general bf16 [M,K] x [K,N], U(-1,1) inputs; config "8192" (default),
+// "batched" (8 x 4096^3) or "MxNxK".  Validation samples 4096 outputs.
+static int run_gemm(const remora_b200_opts* o, remora_b200_report* r, cudaStream_t st) {
+  int64_t batch = 1, M = 8192, N = 8192, K = 8192;
+  if (o && o->config && *o->config) {
+    std::string c = o->config;
+    long long a = 0, b2 = 0, k = 0;
+    if (c == "batched") {
+      batch = 8; M = N = K = 4096;
+    } else if (sscanf(c.c_str(), "%lldx%lldx%lld", &a, &b2, &k) == 3) {
+      M = a; N = b2; K = k;
+    } else if (c != "8192") {
+      return fail(REMORA_B200_ERR_INVALID, "gemm: unknown config '%s'", c.c_str());
+    }
+  }
+  const uint64_t seed = o && o->seed ? o->seed : 42;
+  DevBuf A, B, C;
+  int rc;
+  if ((rc = A.alloc(batch * M * K * 2)) || (rc = B.alloc(batch * K * N * 2)) ||
+      (rc = C.alloc(batch * M * N * 2)))
+    return rc;
+  if ((rc = remora_b200_fill_uniform(A.p, batch * M * K, 1, stream_key(seed, 10), -1, 1, st)))
+    return rc;
+  if ((rc = remora_b200_fill_uniform(B.p, batch * K * N, 1, stream_key(seed, 11), -1, 1, st)))
+    return rc;
+  double ms = 0;
+  rc = time_iters(o, st, [&] {
+    return remora_b200_gemm_bf16(A.p, B.p, C.p, batch, M, N, K, K, N, N, M * K, K * N, M * N,
+                                 REMORA_B200_B_KN, st);
+  }, &ms);
+  if (rc) return rc;
+  ErrStat e;
+  if (o && o->validate) {
+    std::vector<uint16_t> hA(batch * M * K), hB(batch * K * N), hC(batch * M * N);
+    RB_CUDA(cudaMemcpy(hA.data(), A.p, hA.size() * 2, cudaMemcpyDeviceToHost));
+    RB_CUDA(cudaMemcpy(hB.data(), B.p, hB.size() * 2, cudaMemcpyDeviceToHost));
+    RB_CUDA(cudaMemcpy(hC.data(), C.p, hC.size() * 2, cudaMemcpyDeviceToHost));
+    const double floor = 1e-3 * std::sqrt((double)K);  // |C| scales as sqrt(K)/3
+    uint64_t key = stream_key(seed, 99);
+    for (int s2 = 0; s2 < 4096; ++s2) {
+      uint64_t h = host_mix64(key + (uint64_t)s2 * 0x9E3779B97F4A7C15ull);
+      int64_t b = (int64_t)(h % (uint64_t)batch);
+      int64_t i = (int64_t)((h >> 16) % (uint64_t)M), j = (int64_t)((h >> 40) % (uint64_t)N);
+      float acc = 0.0f;
+      for (int64_t k = 0; k < K; ++k)
+        acc += bf16_to_f32(hA[b * M * K + i * K + k]) * bf16_to_f32(hB[b * K * N + k * N + j]);
+      e.add(bf16_to_f32(hC[b * M * N + i * N + j]), acc, floor);
+    }
+  }
+  finish(r, ms, 2.0 * batch * M * N * K, e, 2e-2, o ? o->validate : 0, "gemm bf16", "TFLOP/s");
+  return REMORA_B200_OK;
+}
+
+}  // namespace rb
+
+extern "C" const char* remora_b200_last_error(void) { return rb::t_last_error; }
+
+extern "C" int remora_b200_version(void) { return 100; }
+
+extern "C" int remora_b200_recognise(const char* test) {
+  if (!test) return 0;
+  std::string t = test;
+  return t == "elementwise" || t == "projection" || t == "elementwise_chain" || t == "gemm";
+}
+
+extern "C" int remora_b200_run_test(const char* test, const remora_b200_opts* o,
+                                    remora_b200_report* r) {
+  using namespace rb;
+  clear_error();
+  RB_CHECK_ARG(test && r, "run_test: null argument");
+  memset(r, 0, sizeof(*r));
+  RB_CUDA(cudaSetDevice(o ? o->device : 0));
+  cudaStream_t st;
+  RB_CUDA(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  std::string t = test;
+  int rc;
+  if (t == "elementwise")
+    rc = run_elementwise(o, r, st);
+  else if (t == "projection")
+    rc = run_projection(o, r, st);
+  else if (t == "elementwise_chain")
+    rc = run_chain(o, r, st);
+  else if (t == "gemm")
+    rc = run_gemm(o, r, st);
+  else
+    rc = fail(REMORA_B200_ERR_UNSUPPORTED, "--run-gpu for test '%s' not recognised", test);
+  cudaStreamDestroy(st);
+  if (rc == REMORA_B200_OK && !r->passed)
+    rc = fail(REMORA_B200_ERR_PARITY, "%s", r->detail);
+  return rc;
+}

@@ -1,0 +1,7 @@
+// lib.cu -- single translation unit of libremora_b200.so.  The kernels share
+// one device error word (rb::g_device_error), so they are compiled together.
+#include "runtime.cuh"
+#include "elementwise.cu"
+#include "gemm.cu"
+#include "gemm_f32.cu"
+#include "dispatch.cu"
