@@ -135,9 +135,9 @@ extern "C" int remora_b200_relu_bias_f32(const float* x, const float* bias, floa
                                          int64_t rows, int64_t d, void* stream) {
   clear_error();
   RB_CHECK_ARG(rows >= 0 && d > 0, "relu_bias: rows=%lld d=%lld", (long long)rows, (long long)d);
-  RB_CHECK_ARG(x && bias && out, "relu_bias: null pointer");
   int64_t n = rows * d;
   if (n == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(x && bias && out, "relu_bias: null pointer");
   cudaStream_t st = as_stream(stream);
   if (d % 4 == 0 && aligned16(x) && aligned16(bias) && aligned16(out)) {
     int64_t n4 = n / 4;
@@ -155,8 +155,8 @@ extern "C" int remora_b200_scale_add_exp_f32(const float* s, const float* b, flo
                                              int64_t n, float scale, void* stream) {
   clear_error();
   RB_CHECK_ARG(n >= 0, "scale_add_exp: n=%lld", (long long)n);
-  RB_CHECK_ARG(s && b && out, "scale_add_exp: null pointer");
   if (n == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(s && b && out, "scale_add_exp: null pointer");
   cudaStream_t st = as_stream(stream);
   int64_t head = 0;
   if (aligned16(s) && aligned16(b) && aligned16(out)) {

@@ -253,13 +253,13 @@ static int gemm_bf16_launch(const void* A, const void* B, void* C, int64_t batch
                             int64_t sa, int64_t sb, int64_t sc, int b_layout,
                             cudaStream_t st) {
   using namespace gemm;
-  RB_CHECK_ARG(A && B && C, "gemm_bf16: null pointer");
   RB_CHECK_ARG(batch >= 1 && M >= 0 && N >= 0 && K >= 0, "gemm_bf16: bad sizes");
   RB_CHECK_ARG(b_layout == REMORA_B200_B_KN || b_layout == REMORA_B200_B_NK,
                "gemm_bf16: bad b_layout %d", b_layout);
   RB_CHECK_ARG(M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31) && batch < (1ll << 31),
                "gemm_bf16: sizes exceed 2^31");
   if (M == 0 || N == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(C && (K == 0 || (A && B)), "gemm_bf16: null pointer");
   const bool kn = b_layout == REMORA_B200_B_KN;
   RB_CHECK_ARG(lda >= K && ldc >= N && ldb >= (kn ? N : K), "gemm_bf16: leading dims too small");
   if (K == 0) {

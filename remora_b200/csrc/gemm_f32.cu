@@ -80,7 +80,6 @@ extern "C" int remora_b200_gemm_f32_exact(const float* A, const float* B, float*
                                           int64_t ldc, int b_layout, void* stream) {
   using namespace rb;
   clear_error();
-  RB_CHECK_ARG(A && B && C, "gemm_f32_exact: null pointer");
   RB_CHECK_ARG(M >= 0 && N >= 0 && K >= 0 && M < (1 << 30) && N < (1 << 30) && K < (1 << 30),
                "gemm_f32_exact: bad sizes");
   RB_CHECK_ARG(b_layout == REMORA_B200_B_KN || b_layout == REMORA_B200_B_NK,
@@ -89,6 +88,7 @@ extern "C" int remora_b200_gemm_f32_exact(const float* A, const float* B, float*
   RB_CHECK_ARG(lda >= K && ldc >= N && ldb >= (kn ? N : K),
                "gemm_f32_exact: leading dims too small");
   if (M == 0 || N == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(C && (K == 0 || (A && B)), "gemm_f32_exact: null pointer");
   dim3 grid((unsigned)((N + F32_TN - 1) / F32_TN), (unsigned)((M + F32_TM - 1) / F32_TM));
   RB_CHECK_ARG(grid.y < 65536, "gemm_f32_exact: M too large");
   cudaStream_t st = as_stream(stream);

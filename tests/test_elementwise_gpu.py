@@ -43,10 +43,10 @@ def test_scale_add_exp_parity(rb, orc, n):
 def test_scale_add_exp_unaligned_views(rb, orc):
     s = torch.from_numpy(orc.normal("scores", (1027,))).cuda()
     b = torch.from_numpy(orc.normal("bias", (1027,))).cuda()
-    out = torch.empty(1027, device="cuda")
-    rb.scale_add_exp(s[1:], b[1:], 0.125, out=out[2:1028 - 1])
+    out = torch.empty(1030, device="cuda")
+    rb.scale_add_exp(s[1:], b[1:], 0.125, out=out[2:1028])
     ref = orc.scale_add_exp(s[1:].cpu().numpy(), b[1:].cpu().numpy(), 0.125)
-    got = out[2:1026].cpu().numpy()
+    got = out[2:1028].cpu().numpy()
     assert np.max(np.abs(got - ref) / np.abs(ref)) <= 1e-5
 
 

@@ -15,7 +15,7 @@ def _inputs(orc, batch, M, N, K, b_nk=False, seed=42):
     return a, b
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (200, 300, 136), (1, 8, 8), (129, 264, 72),
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (200, 296, 136), (1, 8, 8), (129, 264, 72),
                                    (256, 512, 1024), (384, 40, 520), (17, 1000, 16)])
 def test_gemm_bf16_full_parity(rb, orc, M, N, K):
     a, b = _inputs(orc, 1, M, N, K)
@@ -85,6 +85,9 @@ def test_gemm_rejects_misaligned(rb):
     with pytest.raises(rb.RemoraError) as e:
         rb.gemm(A[:, :30], B[:30])  # K = 30 is not a multiple of 8
     assert e.value.code == rb.ERR_INVALID
+    B2 = torch.zeros(32, 300, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(rb.RemoraError):
+        rb.gemm(A[:, :32], B2)  # N = 300 breaks the 16-byte row rule of TMA
 
 
 def test_run_test_gemm_full_size(rb):
