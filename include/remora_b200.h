@@ -79,7 +79,7 @@ typedef struct remora_b200_report {
 
 /* 1 if `test` (the --test= kind) is handled by this library, else 0.
  * Kinds: "elementwise" (gpu_tests.cpp:35-95), "projection"
- * (cpu_tests.cpp:65-97), "elementwise_chain", "gemm". */
+ * (cpu_tests.cpp:65-97), "elementwise_chain", "gemm", "attention". */
 int remora_b200_recognise(const char* test);
 
 /* Runs the recognised program end to end on `o->device`: allocates its own
@@ -132,6 +132,20 @@ int remora_b200_gemm_bf16(const void* A, const void* B, void* C, int64_t batch, 
 int remora_b200_gemm_f32_exact(const float* A, const float* B, float* C, int64_t M, int64_t N,
                                int64_t K, int64_t lda, int64_t ldb, int64_t ldc, int b_layout,
                                void* stream);
+
+/* ------------------------------------------------------------------------
+ * Softmax attention (no counterpart program in the reference: README.md:12
+ * lists FlashAttention as in progress; this is the backend's fused form)
+ * --------------------------------------------------------------------- */
+
+/* out = softmax(q k^T * scale [+ causal mask]) v per (batch, head), bf16
+ * q, k, v, out [batch, heads, seq, head_dim] contiguous; fp32 softmax
+ * statistics, P rounded to bf16 for the second product.  head_dim must be
+ * 128; seq is arbitrary (rows past seq are masked).  causal != 0 masks key
+ * j > query i. */
+int remora_b200_attention_fwd_bf16(const void* q, const void* k, const void* v, void* out,
+                                   int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
+                                   int causal, float scale, void* stream);
 
 /* ------------------------------------------------------------------------
  * Seeded input generator (device side of the counter-based generator the

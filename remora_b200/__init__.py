@@ -67,6 +67,7 @@ _SIGNATURES = {
     "remora_b200_scale_add_exp_f32": ([P, P, P, I64, F, P], I),
     "remora_b200_gemm_bf16": ([P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I, P], I),
     "remora_b200_gemm_f32_exact": ([P, P, P, I64, I64, I64, I64, I64, I64, I, P], I),
+    "remora_b200_attention_fwd_bf16": ([P, P, P, P, I64, I64, I64, I64, I, F, P], I),
     "remora_b200_fill_normal": ([P, I64, I, U64, D, D, P], I),
     "remora_b200_fill_uniform": ([P, I64, I, U64, D, D, P], I),
 }
@@ -204,6 +205,25 @@ def gemm_f32_exact(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = 
     _check(lib().remora_b200_gemm_f32_exact(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K,
                                             a.stride(0), b.stride(0), out.stride(0), b_layout,
                                             _stream(a)))
+    return out
+
+
+# ---------------------------------------------------------------- attention
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True,
+              scale: float | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """softmax(q k^T * scale [+ causal mask]) v; q, k, v bf16 [B, H, S, 128]."""
+    _dev(q, k, v)
+    _bf16(q, k, v)
+    if q.dim() != 4 or q.shape != k.shape or q.shape != v.shape:
+        raise ValueError("q, k, v must be [B, H, S, D] of one shape")
+    B, H, S, Dh = q.shape
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    out = torch.empty_like(q) if out is None else out
+    if scale is None:
+        scale = Dh ** -0.5
+    _check(lib().remora_b200_attention_fwd_bf16(q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                                out.data_ptr(), B, H, S, Dh, int(causal),
+                                                float(scale), _stream(q)))
     return out
 
 

@@ -244,6 +244,73 @@ static int run_gemm(const remora_b200_opts* o, remora_b200_report* r, cudaStream
   return REMORA_B200_OK;
 }
 
+// Causal softmax attention, bf16 [B,H,S,128] N(0,1); config "4x32x4096"
+// (default) or "BxHxS"; validation: 64 (head, row) samples, full rows of
+// the output against a double-precision softmax on the host, normwise
+// relative error per row (max |g - r| / max |r|).
+static int run_attention(const remora_b200_opts* o, remora_b200_report* r, cudaStream_t st) {
+  long long B = 4, H = 32, S = 4096;
+  const int64_t Dh = 128;
+  if (o && o->config && *o->config) {
+    if (sscanf(o->config, "%lldx%lldx%lld", &B, &H, &S) != 3)
+      return fail(REMORA_B200_ERR_INVALID, "attention: unknown config '%s'", o->config);
+  }
+  const uint64_t seed = o && o->seed ? o->seed : 42;
+  const int64_t n = B * H * S * Dh;
+  DevBuf q, k, v, out;
+  int rc;
+  if ((rc = q.alloc(n * 2)) || (rc = k.alloc(n * 2)) || (rc = v.alloc(n * 2)) ||
+      (rc = out.alloc(n * 2)))
+    return rc;
+  if ((rc = remora_b200_fill_normal(q.p, n, 1, stream_key(seed, 20), 0, 1, st)) ||
+      (rc = remora_b200_fill_normal(k.p, n, 1, stream_key(seed, 21), 0, 1, st)) ||
+      (rc = remora_b200_fill_normal(v.p, n, 1, stream_key(seed, 22), 0, 1, st)))
+    return rc;
+  const float scale = 1.0f / sqrtf((float)Dh);
+  double ms = 0;
+  rc = time_iters(o, st, [&] {
+    return remora_b200_attention_fwd_bf16(q.p, k.p, v.p, out.p, B, H, S, Dh, 1, scale, st);
+  }, &ms);
+  if (rc) return rc;
+  ErrStat e;
+  if (o && o->validate) {
+    std::vector<uint16_t> hq(n), hk(n), hv(n), ho(n);
+    RB_CUDA(cudaMemcpy(hq.data(), q.p, n * 2, cudaMemcpyDeviceToHost));
+    RB_CUDA(cudaMemcpy(hk.data(), k.p, n * 2, cudaMemcpyDeviceToHost));
+    RB_CUDA(cudaMemcpy(hv.data(), v.p, n * 2, cudaMemcpyDeviceToHost));
+    RB_CUDA(cudaMemcpy(ho.data(), out.p, n * 2, cudaMemcpyDeviceToHost));
+    std::vector<double> pr(S), acc(Dh);
+    uint64_t key = stream_key(seed, 98);
+    for (int s2 = 0; s2 < 64; ++s2) {
+      uint64_t h = host_mix64(key + (uint64_t)s2 * 0x9E3779B97F4A7C15ull);
+      int64_t bh = (int64_t)(h % (uint64_t)(B * H)), i = (int64_t)((h >> 20) % (uint64_t)S);
+      const uint16_t* Q = hq.data() + (bh * S + i) * Dh;
+      double m = -1e300;
+      for (int64_t j = 0; j <= i; ++j) {
+        const uint16_t* Kr = hk.data() + (bh * S + j) * Dh;
+        double d = 0;
+        for (int64_t c = 0; c < Dh; ++c) d += (double)bf16_to_f32(Q[c]) * bf16_to_f32(Kr[c]);
+        pr[j] = d * scale;
+        m = std::max(m, pr[j]);
+      }
+      double l = 0;
+      for (int64_t j = 0; j <= i; ++j) { pr[j] = std::exp(pr[j] - m); l += pr[j]; }
+      std::fill(acc.begin(), acc.end(), 0.0);
+      for (int64_t j = 0; j <= i; ++j) {
+        const uint16_t* Vr = hv.data() + (bh * S + j) * Dh;
+        for (int64_t c = 0; c < Dh; ++c) acc[c] += pr[j] / l * bf16_to_f32(Vr[c]);
+      }
+      double mx = 0;
+      for (int64_t c = 0; c < Dh; ++c) mx = std::max(mx, std::fabs(acc[c]));
+      for (int64_t c = 0; c < Dh; ++c)
+        e.add(bf16_to_f32(ho[(bh * S + i) * Dh + c]), acc[c], std::max(mx, 1e-6));  // normwise per row
+    }
+  }
+  const double flops = 4.0 * B * H * (double)S * S * Dh / 2.0;  // causal half
+  finish(r, ms, flops, e, 2e-2, o ? o->validate : 0, "attention causal bf16", "TFLOP/s");
+  return REMORA_B200_OK;
+}
+
 }  // namespace rb
 
 extern "C" const char* remora_b200_last_error(void) { return rb::t_last_error; }
@@ -253,7 +320,8 @@ extern "C" int remora_b200_version(void) { return 100; }
 extern "C" int remora_b200_recognise(const char* test) {
   if (!test) return 0;
   std::string t = test;
-  return t == "elementwise" || t == "projection" || t == "elementwise_chain" || t == "gemm";
+  return t == "elementwise" || t == "projection" || t == "elementwise_chain" || t == "gemm" ||
+         t == "attention";
 }
 
 extern "C" int remora_b200_run_test(const char* test, const remora_b200_opts* o,
@@ -275,6 +343,8 @@ extern "C" int remora_b200_run_test(const char* test, const remora_b200_opts* o,
     rc = run_chain(o, r, st);
   else if (t == "gemm")
     rc = run_gemm(o, r, st);
+  else if (t == "attention")
+    rc = run_attention(o, r, st);
   else
     rc = fail(REMORA_B200_ERR_UNSUPPORTED, "--run-gpu for test '%s' not recognised", test);
   cudaStreamDestroy(st);

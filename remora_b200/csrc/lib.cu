@@ -4,4 +4,5 @@
 #include "elementwise.cu"
 #include "gemm.cu"
 #include "gemm_f32.cu"
+#include "attention.cu"
 #include "dispatch.cu"
