@@ -52,6 +52,12 @@ const char* remora_b200_last_error(void);
 /* Library version, major*10000 + minor*100 + patch. */
 int remora_b200_version(void);
 
+/* Synchronises the current device and reports (then clears) an error a
+ * kernel recorded on the device since the last check: REMORA_B200_ERR_TIMEOUT
+ * for a bounded device wait that expired, REMORA_B200_ERR_INVALID for a bad
+ * value seen by a kernel (an expert id outside [0, E)). */
+int remora_b200_device_status(void);
+
 /* ------------------------------------------------------------------------
  * Dispatcher (replaces the body of launchOnGpu, gpu_tests.cpp:101-125)
  * --------------------------------------------------------------------- */
@@ -146,6 +152,73 @@ int remora_b200_gemm_f32_exact(const float* A, const float* B, float* C, int64_t
 int remora_b200_attention_fwd_bf16(const void* q, const void* k, const void* v, void* out,
                                    int64_t batch, int64_t heads, int64_t seq, int64_t head_dim,
                                    int causal, float scale, void* stream);
+
+/* ------------------------------------------------------------------------
+ * MoE layer (mlir/stablehlo/mixtral_moe_layer.mlir:8-68; simple_moe.mlir:16-35)
+ * T tokens, D d_model, F ffn dim, E experts, k slots per token.
+ * --------------------------------------------------------------------- */
+
+/* Router: logits[t, e] = sum_d x[t, d] * wr[d, e], accumulated in fp32 in
+ * increasing d from +0.0 (the loop order of the lowered dot_general,
+ * mixtral_moe_layer.mlir:12), so idx is bit-identical to that loop nest;
+ * top-k (:13, mhlo.topk: larger first, NaN first, ties to the lower
+ * expert), then w = softmax over the k selected logits (:14-24).
+ * x bf16 [T, D], wr bf16 [D, E]; idx int32 [T, k], w f32 [T, k].
+ * E <= 256, k <= min(E, 16), D % 8 == 0. */
+int remora_b200_moe_router_topk_bf16(const void* x, const void* wr, int64_t T, int64_t D, int E,
+                                     int k, int32_t* idx, float* w, void* stream);
+
+/* Bytes of device workspace remora_b200_moe_dispatch needs. */
+size_t remora_b200_moe_dispatch_workspace_bytes(int64_t T, int k, int E);
+
+/* Dispatch: the sparse form of the one-hot scatter of
+ * mixtral_moe_layer.mlir:28-31 / :70-78.  counts[E], offsets[E+1]
+ * (exclusive scan), perm[T*k] = t*k + j of the row at each position (rows
+ * grouped by expert, each expert's rows in (token, slot) order),
+ * inv[t*k + j] = its position.  Deterministic.  An expert id outside
+ * [0, E) is reported as a device error by the next synchronising call. */
+int remora_b200_moe_dispatch(const int32_t* idx, int64_t T, int k, int E, int32_t* counts,
+                             int32_t* offsets, int32_t* perm, int32_t* inv, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* xs[p, :] = x[perm[p] / k, :] for p < rows (bf16 rows, D % 8 == 0). */
+int remora_b200_moe_gather(const void* x, const int32_t* perm, int64_t rows, int k, int64_t D,
+                           void* xs, void* stream);
+
+/* Grouped expert GEMM with the SwiGLU epilogue (mixtral_moe_layer.mlir:32-41;
+ * the outlined @expert_slot_N body, compiler/passes/ExpertOutlining.cpp:177-279):
+ * for rows r of expert e (offsets[e] <= r < offsets[e+1]),
+ * h[r, :] = silu(xs[r] . wg[e]) * (xs[r] . wu[e]), silu(g) = g / (1 + exp(-g)).
+ * xs bf16 [rows, D]; wg, wu bf16 [E, D, F]; h bf16 [rows, F].
+ * D % 8 == 0, F % 128 == 0; offsets on the device. */
+int remora_b200_grouped_gemm_swiglu_bf16(const void* xs, const void* wg, const void* wu, void* h,
+                                         const int32_t* offsets, int64_t rows, int64_t D,
+                                         int64_t F, int E, void* stream);
+
+/* Grouped expert GEMM (the down projection, mixtral_moe_layer.mlir:42):
+ * y[r, :] = a[r] . w[e] for the rows of expert e.  a bf16 [rows, K],
+ * w bf16 [E, K, N], y bf16 [rows, N]; K % 8 == 0, N % 256 == 0. */
+int remora_b200_grouped_gemm_bf16(const void* a, const void* w, void* y, const int32_t* offsets,
+                                  int64_t rows, int64_t K, int64_t N, int E, void* stream);
+
+/* Combine (mixtral_moe_layer.mlir:43-46, :52-55): out[t, :] =
+ * bf16(0 + w[t,0]*y[inv[t,0]] + w[t,1]*y[inv[t,1]] + ...), slot order, each
+ * product and sum rounded separately.  y bf16 [T*k, D]; out bf16 [T, D]. */
+int remora_b200_moe_combine_bf16(const void* y, const int32_t* inv, const float* w, int64_t T,
+                                 int k, int64_t D, void* out, void* stream);
+
+/* Bytes of device workspace remora_b200_moe_layer_bf16 needs. */
+size_t remora_b200_moe_workspace_bytes(int64_t T, int64_t D, int64_t F, int E, int k);
+
+/* The whole MoE layer: router -> dispatch -> gather -> SwiGLU grouped GEMM
+ * -> down grouped GEMM -> combine, stream-ordered, no host synchronisation.
+ * x bf16 [T, D]; wr bf16 [D, E]; wg, wu bf16 [E, D, F]; wd bf16 [E, F, D];
+ * out bf16 [T, D].  F % 128 == 0, D % 256 == 0.  The workspace (caller
+ * owned, 16-byte aligned) holds the routing tables and the dispatched
+ * activations. */
+int remora_b200_moe_layer_bf16(const void* x, const void* wr, const void* wg, const void* wu,
+                               const void* wd, void* out, int64_t T, int64_t D, int64_t F, int E,
+                               int k, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * Seeded input generator (device side of the counter-based generator the

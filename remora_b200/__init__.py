@@ -68,6 +68,17 @@ _SIGNATURES = {
     "remora_b200_gemm_bf16": ([P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I, P], I),
     "remora_b200_gemm_f32_exact": ([P, P, P, I64, I64, I64, I64, I64, I64, I, P], I),
     "remora_b200_attention_fwd_bf16": ([P, P, P, P, I64, I64, I64, I64, I, F, P], I),
+    "remora_b200_moe_router_topk_bf16": ([P, P, I64, I64, I, I, P, P, P], I),
+    "remora_b200_moe_dispatch_workspace_bytes": ([I64, I, I], ctypes.c_size_t),
+    "remora_b200_moe_dispatch": ([P, I64, I, I, P, P, P, P, P, ctypes.c_size_t, P], I),
+    "remora_b200_moe_gather": ([P, P, I64, I, I64, P, P], I),
+    "remora_b200_grouped_gemm_swiglu_bf16": ([P, P, P, P, P, I64, I64, I64, I, P], I),
+    "remora_b200_grouped_gemm_bf16": ([P, P, P, P, I64, I64, I64, I, P], I),
+    "remora_b200_moe_combine_bf16": ([P, P, P, I64, I, I64, P, P], I),
+    "remora_b200_moe_workspace_bytes": ([I64, I64, I64, I, I], ctypes.c_size_t),
+    "remora_b200_moe_layer_bf16": ([P, P, P, P, P, P, I64, I64, I64, I, I, P, ctypes.c_size_t, P],
+                                   I),
+    "remora_b200_device_status": ([], I),
     "remora_b200_fill_normal": ([P, I64, I, U64, D, D, P], I),
     "remora_b200_fill_uniform": ([P, I64, I, U64, D, D, P], I),
 }
@@ -225,6 +236,127 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
                                                 out.data_ptr(), B, H, S, Dh, int(causal),
                                                 float(scale), _stream(q)))
     return out
+
+
+# ---------------------------------------------------------------------- MoE
+def _i32(*ts):
+    for t in ts:
+        if t.dtype != torch.int32 or not t.is_contiguous():
+            raise TypeError("expected a contiguous int32 tensor")
+
+
+def moe_router_topk(x: torch.Tensor, wr: torch.Tensor, k: int):
+    """Router logits (increasing-d fp32), top-k indices and softmax weights."""
+    _dev(x, wr)
+    _bf16(x, wr)
+    T, D = x.shape
+    E = wr.shape[1]
+    x, wr = x.contiguous(), wr.contiguous()
+    idx = torch.empty((T, k), dtype=torch.int32, device=x.device)
+    w = torch.empty((T, k), dtype=torch.float32, device=x.device)
+    _check(lib().remora_b200_moe_router_topk_bf16(x.data_ptr(), wr.data_ptr(), T, D, E, k,
+                                                  idx.data_ptr(), w.data_ptr(), _stream(x)))
+    return idx, w
+
+
+def moe_dispatch(idx: torch.Tensor, E: int):
+    """counts[E], offsets[E+1], perm[T*k], inv[T*k] (stable by expert)."""
+    _dev(idx)
+    _i32(idx)
+    T, k = idx.shape
+    dev = idx.device
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+    offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+    perm = torch.empty(T * k, dtype=torch.int32, device=dev)
+    inv = torch.empty(T * k, dtype=torch.int32, device=dev)
+    nws = lib().remora_b200_moe_dispatch_workspace_bytes(T, k, E)
+    ws = torch.empty(max(nws, 1), dtype=torch.uint8, device=dev)
+    _check(lib().remora_b200_moe_dispatch(idx.data_ptr(), T, k, E, counts.data_ptr(),
+                                          offsets.data_ptr(), perm.data_ptr(), inv.data_ptr(),
+                                          ws.data_ptr(), nws, _stream(idx)))
+    return counts, offsets, perm, inv
+
+
+def moe_gather(x: torch.Tensor, perm: torch.Tensor, k: int) -> torch.Tensor:
+    _dev(x, perm)
+    _i32(perm)
+    T, D = x.shape
+    rows = perm.numel()
+    xs = torch.empty((rows, D), dtype=x.dtype, device=x.device)
+    _check(lib().remora_b200_moe_gather(x.contiguous().data_ptr(), perm.data_ptr(), rows, k, D,
+                                        xs.data_ptr(), _stream(x)))
+    return xs
+
+
+def grouped_gemm_swiglu(xs: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor,
+                        offsets: torch.Tensor) -> torch.Tensor:
+    """h = silu(xs . wg[e]) * (xs . wu[e]) over each expert's row segment."""
+    _dev(xs, wg, wu, offsets)
+    _bf16(xs, wg, wu)
+    _i32(offsets)
+    rows, D = xs.shape
+    E, _, F = wg.shape
+    h = torch.empty((rows, F), dtype=torch.bfloat16, device=xs.device)
+    _check(lib().remora_b200_grouped_gemm_swiglu_bf16(
+        xs.contiguous().data_ptr(), wg.contiguous().data_ptr(), wu.contiguous().data_ptr(),
+        h.data_ptr(), offsets.data_ptr(), rows, D, F, E, _stream(xs)))
+    return h
+
+
+def grouped_gemm(a: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
+    """y = a . w[e] over each expert's row segment (w [E, K, N])."""
+    _dev(a, w, offsets)
+    _bf16(a, w)
+    _i32(offsets)
+    rows, K = a.shape
+    E, _, N = w.shape
+    y = torch.empty((rows, N), dtype=torch.bfloat16, device=a.device)
+    _check(lib().remora_b200_grouped_gemm_bf16(a.contiguous().data_ptr(), w.contiguous().data_ptr(),
+                                               y.data_ptr(), offsets.data_ptr(), rows, K, N, E,
+                                               _stream(a)))
+    return y
+
+
+def moe_combine(y: torch.Tensor, inv: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    _dev(y, inv, w)
+    _i32(inv)
+    T, k = w.shape
+    D = y.shape[1]
+    out = torch.empty((T, D), dtype=torch.bfloat16, device=y.device)
+    _check(lib().remora_b200_moe_combine_bf16(y.contiguous().data_ptr(), inv.data_ptr(),
+                                              w.contiguous().data_ptr(), T, k, D, out.data_ptr(),
+                                              _stream(y)))
+    return out
+
+
+def moe_workspace_bytes(T: int, D: int, F: int, E: int, k: int) -> int:
+    return int(lib().remora_b200_moe_workspace_bytes(T, D, F, E, k))
+
+
+def moe_layer(x: torch.Tensor, wr: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor,
+              wd: torch.Tensor, k: int, out: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The whole MoE layer (router, dispatch, SwiGLU experts, combine), bf16."""
+    _dev(x, wr, wg, wu, wd)
+    _bf16(x, wr, wg, wu, wd)
+    T, D = x.shape
+    E, _, F = wg.shape
+    need = moe_workspace_bytes(T, D, F, E, k)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    out = torch.empty((T, D), dtype=torch.bfloat16, device=x.device) if out is None else out
+    _check(lib().remora_b200_moe_layer_bf16(
+        x.contiguous().data_ptr(), wr.contiguous().data_ptr(), wg.contiguous().data_ptr(),
+        wu.contiguous().data_ptr(), wd.contiguous().data_ptr(), out.data_ptr(), T, D, F, E, k,
+        workspace.data_ptr(), workspace.numel(), _stream(x)))
+    return out
+
+
+def synchronize_and_check(device=None) -> None:
+    """Synchronises the device and raises if a kernel reported an error
+    (bad expert id, timed-out device wait)."""
+    torch.cuda.synchronize(device)
+    _check(lib().remora_b200_device_status())
 
 
 # ---------------------------------------------------------- seeded inputs

@@ -317,6 +317,18 @@ extern "C" const char* remora_b200_last_error(void) { return rb::t_last_error; }
 
 extern "C" int remora_b200_version(void) { return 100; }
 
+extern "C" int remora_b200_device_status(void) {
+  rb::clear_error();
+  int v = 0, zero = 0;
+  RB_CUDA(cudaDeviceSynchronize());
+  RB_CUDA(cudaMemcpyFromSymbol(&v, rb::g_device_error, sizeof(int)));
+  if (v == 0) return REMORA_B200_OK;
+  RB_CUDA(cudaMemcpyToSymbol(rb::g_device_error, &zero, sizeof(int)));
+  if (v == 1) return rb::fail(REMORA_B200_ERR_TIMEOUT, "a device-side wait timed out");
+  if (v == 2) return rb::fail(REMORA_B200_ERR_INVALID, "an expert index was outside [0, E)");
+  return rb::fail(REMORA_B200_ERR_INVALID, "device reported error %d", v);
+}
+
 extern "C" int remora_b200_recognise(const char* test) {
   if (!test) return 0;
   std::string t = test;

@@ -5,4 +5,7 @@
 #include "gemm.cu"
 #include "gemm_f32.cu"
 #include "attention.cu"
+#include "moe.cu"
+#include "moe_gemm.cu"
+#include "moe_host.cu"
 #include "dispatch.cu"

@@ -1,0 +1,268 @@
+// moe_gemm.cu -- persistent grouped GEMMs of the MoE experts on tcgen05.
+//
+// Expert e owns rows [offsets[e], offsets[e+1]) of the dispatched activation
+// matrix (expert-contiguous, written by the dispatch kernels).  Its FFN
+// (mixtral_moe_layer.mlir:32-42; the outlined @expert_slot_N of
+// compiler/passes/ExpertOutlining.cpp:177-279) runs as two grouped GEMMs:
+//   kSwiGLU = true   H[r, :] = silu(X[r] . Wg[e]) * (X[r] . Wu[e])   [rows, F]
+//                    gate and up tiles (128 columns each) accumulate side by
+//                    side in TMEM; the epilogue applies
+//                    silu(g) = g * (1 / (1 + exp(-g))) (:34-41) and stores bf16.
+//   kSwiGLU = false  Y[r, :] = H[r] . Wd[e]                           [rows, D]
+// Weights are [E, K, N] with N contiguous, consumed MN-major by the smem
+// descriptors straight from the reference layout (no interleave pass).
+// The tile list (expert, 128-row tile, column tile) is derived on the
+// device from the expert offsets[] written by the dispatch scan, so
+// variable per-expert row counts need no host round trip.  Rows of a tile
+// past its expert's end are computed and discarded (guarded stores).
+// Warp roles as in gemm.cu: TMA producer, MMA issuer, 4 epilogue warps,
+// double-buffered TMEM accumulators.
+#include "runtime.cuh"
+
+namespace rb {
+namespace moe {
+
+constexpr int GBM = 128, GBK = 64, GStages = 4, GGroupM = 16, GMaxE = 256;
+constexpr int GThreads = 192;
+constexpr uint32_t GABytes = GBM * GBK * 2;        // 16 KB
+constexpr uint32_t GBBytes = 256 * GBK * 2;        // 32 KB: 4 boxes of [64 K x 64 N]
+constexpr uint32_t GStageBytes = GABytes + GBBytes;
+constexpr uint32_t GBarOffset = GStages * GStageBytes;
+constexpr uint32_t GSmemBytes = GBarOffset + 256 + 2 * (GMaxE + 1) * 4 + 1024;
+
+struct GroupShape {
+  int K, N, E;
+  int tiles_n;       // N / (columns per tile)
+  int num_kb;
+  const int32_t* offsets;  // [E+1] device: expert row segments
+  uint16_t* out;           // [rows, N] bf16
+};
+
+struct GSmem {
+  uint64_t full[GStages], empty[GStages];
+  uint64_t tmem_full[2], tmem_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  int total_tiles;
+};
+
+struct TileInfo {
+  int e, r0, r_end, n;
+};
+
+__device__ __forceinline__ TileInfo group_tile(const GroupShape& s, const int* mt, const int* off,
+                                               int total_mt, int t) {
+  const int span = GGroupM * s.tiles_n;
+  const int grp = t / span;
+  const int first = grp * GGroupM;
+  const int gm = min(total_mt - first, GGroupM);
+  const int rr = t - grp * span;
+  const int g = first + rr % gm;
+  TileInfo ti;
+  ti.n = rr / gm;
+  int lo = 0, hi = s.E;  // last e with mt[e] <= g
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (mt[mid] <= g) lo = mid; else hi = mid;
+  }
+  ti.e = lo;
+  ti.r0 = off[lo] + (g - mt[lo]) * GBM;
+  ti.r_end = off[lo + 1];
+  return ti;
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-g * 1.4426950408889634f));
+  return (g * __frcp_rn(1.0f + e)) * u;
+}
+
+template <bool kSwiGLU>
+__global__ void __launch_bounds__(GThreads, 1)
+    k_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                   const __grid_constant__ CUtensorMap tmB1, GroupShape s) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  GSmem* sm = reinterpret_cast<GSmem*>(smem + GBarOffset);
+  int* s_mt = reinterpret_cast<int*>(smem + GBarOffset + 256);
+  int* s_off = s_mt + (GMaxE + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  for (int i = threadIdx.x; i <= s.E; i += blockDim.x) s_off[i] = s.offsets[i];
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // m-tile prefix: expert e owns tiles [s_mt[e], s_mt[e+1]) of GBM rows
+    int mt = 0;
+    for (int e = 0; e < s.E; ++e) {
+      s_mt[e] = mt;
+      mt += (s_off[e + 1] - s_off[e] + GBM - 1) / GBM;
+    }
+    s_mt[s.E] = mt;
+    for (int i = 0; i < GStages; ++i) {
+      mbar_init(&sm->full[i], 1);
+      mbar_init(&sm->empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm->tmem_full[i], 1);
+      mbar_init(&sm->tmem_empty[i], 4);
+    }
+    mbar_init(&sm->drain, 1);
+    sm->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = sm->tmem_base;
+  volatile int* abort_flag = &sm->abort_flag;
+  const int total_mt = s_mt[s.E];
+  const int total_tiles = total_mt * s.tiles_n;
+  constexpr int kColsPerTile = kSwiGLU ? 128 : 256;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB0);
+      if (kSwiGLU) tma_prefetch_desc(&tmB1);
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+        const TileInfo ti = group_tile(s, s_mt, s_off, total_mt, t);
+        const int n0 = ti.n * kColsPerTile;
+        for (int kb = 0; kb < s.num_kb; ++kb) {
+          if (!mbar_wait(&sm->empty[stage], phase ^ 1)) { *abort_flag = 1; break; }
+          uint8_t* sa = smem + stage * GStageBytes;
+          uint8_t* sb = sa + GABytes;
+          mbar_arrive_expect_tx(&sm->full[stage], GStageBytes);
+          tma_load_2d(sa, &tmA, &sm->full[stage], kb * GBK, ti.r0);
+          if (kSwiGLU) {
+            for (int c = 0; c < 2; ++c) {
+              tma_load_3d(sb + c * 8192, &tmB0, &sm->full[stage], n0 + c * 64, kb * GBK, ti.e);
+              tma_load_3d(sb + 16384 + c * 8192, &tmB1, &sm->full[stage], n0 + c * 64, kb * GBK,
+                          ti.e);
+            }
+          } else {
+            for (int c = 0; c < 4; ++c)
+              tma_load_3d(sb + c * 8192, &tmB0, &sm->full[stage], n0 + c * 64, kb * GBK, ti.e);
+          }
+          ++issued;
+          if (++stage == GStages) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (*abort_flag) {
+        int st = stage, ph = phase;
+        for (int i = 0; i < GStages && i < issued; ++i) {
+          if (--st < 0) { st = GStages - 1; ph ^= 1; }
+          mbar_wait(&sm->full[st], ph);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = kSwiGLU ? idesc_bf16_f32(GBM, 128, 0, 1)
+                                         : idesc_bf16_f32(GBM, 256, 0, 1);
+      int stage = 0, acc = 0;
+      uint32_t phase = 0, acc_phase = 0;
+      bool issued_any = false;
+      for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+        if (!mbar_wait(&sm->tmem_empty[acc], acc_phase ^ 1)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t d0 = tmem_base + acc * 256;
+        for (int kb = 0; kb < s.num_kb; ++kb) {
+          if (!mbar_wait(&sm->full[stage], phase)) { *abort_flag = 1; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * GStageBytes);
+          const uint32_t sb = sa + GABytes;
+#pragma unroll
+          for (int k = 0; k < GBK / 16; ++k) {
+            const uint64_t adesc = smem_desc_sw128(sa + k * 32, 16, 1024);
+            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            if (kSwiGLU) {
+              mma_bf16_ss(d0, adesc, smem_desc_sw128(sb + k * 2048, 8192, 1024), idesc, accum);
+              mma_bf16_ss(d0 + 128, adesc, smem_desc_sw128(sb + 16384 + k * 2048, 8192, 1024),
+                          idesc, accum);
+            } else {
+              mma_bf16_ss(d0, adesc, smem_desc_sw128(sb + k * 2048, 8192, 1024), idesc, accum);
+            }
+          }
+          issued_any = true;
+          mma_commit(&sm->empty[stage]);
+          if (++stage == GStages) { stage = 0; phase ^= 1; }
+        }
+        if (*abort_flag) break;
+        mma_commit(&sm->tmem_full[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      if (*abort_flag && issued_any) {
+        mma_commit(&sm->drain);
+        mbar_wait(&sm->drain, 0);
+      }
+    }
+  } else {
+    const int lg = warp & 3;
+    const int row = lg * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const TileInfo ti = group_tile(s, s_mt, s_off, total_mt, t);
+      bool got = !*abort_flag && mbar_wait(&sm->tmem_full[acc], acc_phase);
+      if (!__all_sync(0xffffffffu, got)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(lg * 32) << 16) + acc * 256;
+      const int grow = ti.r0 + row;
+      const bool valid = grow < ti.r_end;
+      uint16_t* dst = s.out + (int64_t)grow * s.N + ti.n * kColsPerTile;
+      constexpr int kChunks = kColsPerTile / 32;
+#pragma unroll 1
+      for (int c = 0; c < kChunks; ++c) {
+        uint32_t pk[16];
+        if (kSwiGLU) {
+          uint32_t g[32], u[32];
+          tmem_ld32(t_row + c * 32, g);
+          tmem_ld32(t_row + 128 + c * 32, u);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = pack_bf16x2(silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i])),
+                                silu_mul(__uint_as_float(g[2 * i + 1]),
+                                         __uint_as_float(u[2 * i + 1])));
+        } else {
+          uint32_t v[32];
+          tmem_ld32(t_row + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+        }
+        if (c == kChunks - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sm->tmem_empty[acc]);
+        }
+        if (valid) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace moe
+}  // namespace rb

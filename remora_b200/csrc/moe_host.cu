@@ -1,0 +1,272 @@
+// moe_host.cu -- C ABI launchers of the MoE layer (router, dispatch, gather,
+// grouped expert GEMMs, combine) and the fused layer entry point.
+#include "runtime.cuh"
+
+namespace rb {
+namespace moe {
+
+inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+inline int64_t dispatch_blocks(int64_t n) { return (n + kDispThreads - 1) / kDispThreads; }
+
+int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, int k,
+                  int32_t* idx, float* w, cudaStream_t st) {
+  RB_CHECK_ARG(T >= 0 && D > 0 && E >= 1 && E <= GMaxE && k >= 1 && k <= 16 && k <= E,
+               "router: unsupported sizes (T=%lld D=%lld E=%d k=%d)", (long long)T,
+               (long long)D, E, k);
+  RB_CHECK_ARG(D % 8 == 0, "router: d_model must be a multiple of 8");
+  if (T == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(x && wr && idx && w, "router: null pointer");
+  RB_CHECK_ARG(aligned16(x), "router: x must be 16-byte aligned");
+  RB_CHECK_ARG(T < (1ll << 31) && D < (1ll << 31), "router: sizes exceed 2^31");
+  int G = kRouterThreads / E;
+  if (G > 32) G = 32;
+  if (G < 1) G = 1;
+  const int threads = ((G * E + 31) / 32) * 32;
+  const int TPB = G * kRouterR;
+  const size_t smem = (size_t)(TPB + E) * kRowPad * 2 + (size_t)TPB * E * 4;
+  if (smem > 48 * 1024)
+    RB_CUDA(cudaFuncSetAttribute(k_router_topk, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem));
+  const int64_t grid = (T + TPB - 1) / TPB;
+  k_router_topk<<<(unsigned)grid, threads, smem, st>>>(
+      static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(wr), (int)T, (int)D, E, k, G,
+      idx, w);
+  RB_LAUNCH_CHECK();
+  return REMORA_B200_OK;
+}
+
+size_t dispatch_ws_bytes(int64_t T, int k, int E) {
+  return align256((size_t)dispatch_blocks(T * k) * E * 4);
+}
+
+int dispatch_launch(const int32_t* idx, int64_t T, int k, int E, int32_t* counts,
+                    int32_t* offsets, int32_t* perm, int32_t* inv, int32_t* block_counts,
+                    cudaStream_t st) {
+  const int64_t n = T * k;
+  const int64_t nb = dispatch_blocks(n);
+  RB_CHECK_ARG(nb < (1 << 30), "dispatch: too many entries");
+  if (n == 0) {
+    RB_CHECK_ARG(counts && offsets, "dispatch: null pointer");
+    RB_CUDA(cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st));
+    RB_CUDA(cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (E + 1), st));
+    return REMORA_B200_OK;
+  }
+  k_dispatch_count<<<(unsigned)nb, kDispThreads, E * sizeof(int), st>>>(idx, n, E, block_counts);
+  RB_LAUNCH_CHECK();
+  k_dispatch_scan<<<1, 256, E * sizeof(int), st>>>(block_counts, (int)nb, E, counts, offsets);
+  RB_LAUNCH_CHECK();
+  k_dispatch_scatter<<<(unsigned)nb, kDispThreads, 32 * E * sizeof(int), st>>>(
+      idx, n, E, block_counts, offsets, perm, inv);
+  RB_LAUNCH_CHECK();
+  return REMORA_B200_OK;
+}
+
+int gather_launch(const void* x, const int32_t* perm, int64_t rows, int k, int64_t D, void* xs,
+                  cudaStream_t st) {
+  RB_CHECK_ARG(rows >= 0 && k >= 1 && D > 0 && D % 8 == 0, "gather: bad sizes");
+  if (rows == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(x && perm && xs && aligned16(x) && aligned16(xs),
+               "gather: null or unaligned pointer");
+  const int64_t want = (rows + 7) / 8;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  k_gather_rows<<<(unsigned)(want < cap ? want : cap), 256, 0, st>>>(
+      static_cast<const uint16_t*>(x), perm, rows, k, (int)D, static_cast<uint16_t*>(xs));
+  RB_LAUNCH_CHECK();
+  return REMORA_B200_OK;
+}
+
+// Grouped GEMM over expert row segments.  a [rows, K]; b0 (and b1 for the
+// SwiGLU form) [E, K, N]; out [rows, N].  offsets [E+1] on the device.
+int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, void* out,
+                   const int32_t* offsets, int64_t rows, int64_t K, int64_t N, int E,
+                   cudaStream_t st) {
+  const int cols = swiglu ? 128 : 256;
+  RB_CHECK_ARG(E >= 1 && E <= GMaxE, "grouped_gemm: E=%d unsupported (1..%d)", E, GMaxE);
+  RB_CHECK_ARG(rows >= 0 && K > 0 && N > 0 && K % 8 == 0 && N % cols == 0,
+               "grouped_gemm: need K %% 8 == 0 and N %% %d == 0 (K=%lld N=%lld)", cols,
+               (long long)K, (long long)N);
+  RB_CHECK_ARG(rows < (1ll << 31) && K < (1ll << 31) && N < (1ll << 31),
+               "grouped_gemm: sizes exceed 2^31");
+  if (rows == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(a && b0 && out && offsets && (!swiglu || b1), "grouped_gemm: null pointer");
+  RB_CHECK_ARG(aligned16(a) && aligned16(b0) && aligned16(out) && (!swiglu || aligned16(b1)),
+               "grouped_gemm: pointers must be 16-byte aligned");
+  CUtensorMap tA, tB0, tB1;
+  int rc;
+  {
+    uint64_t d[2] = {(uint64_t)K, (uint64_t)rows};
+    uint64_t s[1] = {(uint64_t)K * 2};
+    uint32_t box[2] = {GBK, GBM};
+    if ((rc = make_tmap(&tA, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, s, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+  }
+  uint64_t d[3] = {(uint64_t)N, (uint64_t)K, (uint64_t)E};
+  uint64_t s[2] = {(uint64_t)N * 2, (uint64_t)K * N * 2};
+  uint32_t box[3] = {64, GBK, 1};
+  if ((rc = make_tmap(&tB0, b0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, d, s, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  if ((rc = make_tmap(&tB1, swiglu ? b1 : b0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, d, s, box,
+                      CU_TENSOR_MAP_SWIZZLE_128B)))
+    return rc;
+  GroupShape sh;
+  sh.K = (int)K;
+  sh.N = (int)N;
+  sh.E = E;
+  sh.tiles_n = (int)(N / cols);
+  sh.num_kb = (int)((K + GBK - 1) / GBK);
+  sh.offsets = offsets;
+  sh.out = static_cast<uint16_t*>(out);
+  // upper bound of the tile count: sum over experts of ceil(n_e / 128)
+  const int64_t max_tiles = (rows / GBM + E) * (int64_t)sh.tiles_n;
+  int grid = num_sms();
+  if (grid > max_tiles) grid = (int)max_tiles;
+  if (swiglu) {
+    RB_CUDA(cudaFuncSetAttribute(k_grouped_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 GSmemBytes));
+    k_grouped_gemm<true><<<grid, GThreads, GSmemBytes, st>>>(tA, tB0, tB1, sh);
+  } else {
+    RB_CUDA(cudaFuncSetAttribute(k_grouped_gemm<false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, GSmemBytes));
+    k_grouped_gemm<false><<<grid, GThreads, GSmemBytes, st>>>(tA, tB0, tB1, sh);
+  }
+  RB_LAUNCH_CHECK();
+  return REMORA_B200_OK;
+}
+
+int combine_launch(const void* y, const int32_t* inv, const float* w, int64_t T, int k,
+                   int64_t D, void* out, cudaStream_t st) {
+  RB_CHECK_ARG(T >= 0 && k >= 1 && k <= 16 && D > 0 && D % 8 == 0, "combine: bad sizes");
+  if (T == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(y && inv && w && out && aligned16(y) && aligned16(out),
+               "combine: null or unaligned pointer");
+  const int64_t want = (T + 7) / 8;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  k_combine<<<(unsigned)(want < cap ? want : cap), 256, 0, st>>>(
+      static_cast<const uint16_t*>(y), inv, w, T, k, (int)D, static_cast<uint16_t*>(out));
+  RB_LAUNCH_CHECK();
+  return REMORA_B200_OK;
+}
+
+// Workspace layout of the fused layer (each piece 256-byte aligned).
+struct LayerWs {
+  int32_t *idx, *counts, *offsets, *perm, *inv, *block_counts;
+  float* w;
+  uint16_t *xs, *h, *y;
+  size_t bytes;
+};
+
+inline LayerWs layer_ws(void* base, int64_t T, int64_t D, int64_t F, int E, int k) {
+  LayerWs L;
+  const int64_t n = T * k;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o += align256(bytes);
+    return static_cast<uint8_t*>(base) + at;
+  };
+  L.idx = reinterpret_cast<int32_t*>(take(n * 4));
+  L.w = reinterpret_cast<float*>(take(n * 4));
+  L.counts = reinterpret_cast<int32_t*>(take(E * 4));
+  L.offsets = reinterpret_cast<int32_t*>(take((E + 1) * 4));
+  L.perm = reinterpret_cast<int32_t*>(take(n * 4));
+  L.inv = reinterpret_cast<int32_t*>(take(n * 4));
+  L.block_counts = reinterpret_cast<int32_t*>(take(dispatch_ws_bytes(T, k, E)));
+  L.xs = reinterpret_cast<uint16_t*>(take(n * D * 2));
+  L.h = reinterpret_cast<uint16_t*>(take(n * F * 2));
+  L.y = reinterpret_cast<uint16_t*>(take(n * D * 2));
+  L.bytes = o;
+  return L;
+}
+
+}  // namespace moe
+}  // namespace rb
+
+using namespace rb;
+using namespace rb::moe;
+
+extern "C" int remora_b200_moe_router_topk_bf16(const void* x, const void* wr, int64_t T,
+                                                int64_t D, int E, int k, int32_t* idx, float* w,
+                                                void* stream) {
+  clear_error();
+  return router_launch(x, wr, T, D, E, k, idx, w, as_stream(stream));
+}
+
+extern "C" size_t remora_b200_moe_dispatch_workspace_bytes(int64_t T, int k, int E) {
+  return dispatch_ws_bytes(T, k, E);
+}
+
+extern "C" int remora_b200_moe_dispatch(const int32_t* idx, int64_t T, int k, int E,
+                                        int32_t* counts, int32_t* offsets, int32_t* perm,
+                                        int32_t* inv, void* workspace, size_t workspace_bytes,
+                                        void* stream) {
+  clear_error();
+  RB_CHECK_ARG(T >= 0 && k >= 1 && E >= 1 && E <= GMaxE, "dispatch: bad sizes");
+  RB_CHECK_ARG(T * k == 0 || (idx && counts && offsets && perm && inv && workspace),
+               "dispatch: null pointer");
+  RB_CHECK_ARG(workspace_bytes >= dispatch_ws_bytes(T, k, E) || T * k == 0,
+               "dispatch: workspace of %zu bytes, %zu needed", workspace_bytes,
+               dispatch_ws_bytes(T, k, E));
+  return dispatch_launch(idx, T, k, E, counts, offsets, perm, inv,
+                         static_cast<int32_t*>(workspace), as_stream(stream));
+}
+
+extern "C" int remora_b200_moe_gather(const void* x, const int32_t* perm, int64_t rows, int k,
+                                      int64_t D, void* xs, void* stream) {
+  clear_error();
+  return gather_launch(x, perm, rows, k, D, xs, as_stream(stream));
+}
+
+extern "C" int remora_b200_grouped_gemm_swiglu_bf16(const void* xs, const void* wg,
+                                                    const void* wu, void* h,
+                                                    const int32_t* offsets, int64_t rows,
+                                                    int64_t D, int64_t F, int E, void* stream) {
+  clear_error();
+  return grouped_launch(true, xs, wg, wu, h, offsets, rows, D, F, E, as_stream(stream));
+}
+
+extern "C" int remora_b200_grouped_gemm_bf16(const void* a, const void* w, void* y,
+                                             const int32_t* offsets, int64_t rows, int64_t K,
+                                             int64_t N, int E, void* stream) {
+  clear_error();
+  return grouped_launch(false, a, w, nullptr, y, offsets, rows, K, N, E, as_stream(stream));
+}
+
+extern "C" int remora_b200_moe_combine_bf16(const void* y, const int32_t* inv, const float* w,
+                                            int64_t T, int k, int64_t D, void* out,
+                                            void* stream) {
+  clear_error();
+  return combine_launch(y, inv, w, T, k, D, out, as_stream(stream));
+}
+
+extern "C" size_t remora_b200_moe_workspace_bytes(int64_t T, int64_t D, int64_t F, int E, int k) {
+  return layer_ws(nullptr, T, D, F, E, k).bytes;
+}
+
+extern "C" int remora_b200_moe_layer_bf16(const void* x, const void* wr, const void* wg,
+                                          const void* wu, const void* wd, void* out, int64_t T,
+                                          int64_t D, int64_t F, int E, int k, void* workspace,
+                                          size_t workspace_bytes, void* stream) {
+  clear_error();
+  RB_CHECK_ARG(T >= 0 && D > 0 && F > 0 && E >= 1 && E <= GMaxE && k >= 1 && k <= 16 && k <= E,
+               "moe_layer: bad sizes");
+  if (T == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(x && wr && wg && wu && wd && out && workspace, "moe_layer: null pointer");
+  LayerWs L = layer_ws(workspace, T, D, F, E, k);
+  RB_CHECK_ARG(workspace_bytes >= L.bytes, "moe_layer: workspace of %zu bytes, %zu needed",
+               workspace_bytes, L.bytes);
+  RB_CHECK_ARG(aligned16(workspace), "moe_layer: workspace must be 16-byte aligned");
+  cudaStream_t st = as_stream(stream);
+  const int64_t n = T * k;
+  int rc;
+  if ((rc = router_launch(x, wr, T, D, E, k, L.idx, L.w, st))) return rc;
+  if ((rc = dispatch_launch(L.idx, T, k, E, L.counts, L.offsets, L.perm, L.inv, L.block_counts,
+                            st)))
+    return rc;
+  if ((rc = gather_launch(x, L.perm, n, k, D, L.xs, st))) return rc;
+  if ((rc = grouped_launch(true, L.xs, wg, wu, L.h, L.offsets, n, D, F, E, st))) return rc;
+  if ((rc = grouped_launch(false, L.h, wd, nullptr, L.y, L.offsets, n, F, D, E, st))) return rc;
+  return combine_launch(L.y, L.inv, L.w, T, k, D, out, st);
+}
