@@ -181,6 +181,22 @@ int remora_b200_moe_dispatch(const int32_t* idx, int64_t T, int k, int E, int32_
                              int32_t* offsets, int32_t* perm, int32_t* inv, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* Same dispatch as remora_b200_moe_dispatch, for callers that cannot
+ * allocate device memory when they dispatch (code running inside a memory
+ * pool it does not own, embedders that fix their memory use at start-up,
+ * latency-critical paths that must not take the allocator's lock).  No
+ * counterpart in the reference.  It allocates nothing: its scratch is a
+ * fixed 1 MiB array inside the library, held by every GPU that loads the
+ * library until the process exits.  A call needing more than
+ * 262144 scratch slots (ceil(T*k / 1024) * E) fails with
+ * REMORA_B200_ERR_INVALID.  All calls on a device share the array, so calls
+ * that overlap on the GPU race; serialise them (e.g. one stream).  The first
+ * call on a device looks up the array's device address; make it before any
+ * stream capture. */
+int remora_b200_moe_dispatch_noalloc(const int32_t* idx, int64_t T, int k, int E,
+                                     int32_t* counts, int32_t* offsets, int32_t* perm,
+                                     int32_t* inv, void* stream);
+
 /* xs[p, :] = x[perm[p] / k, :] for p < rows (bf16 rows, D % 8 == 0). */
 int remora_b200_moe_gather(const void* x, const int32_t* perm, int64_t rows, int k, int64_t D,
                            void* xs, void* stream);

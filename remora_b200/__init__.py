@@ -71,6 +71,7 @@ _SIGNATURES = {
     "remora_b200_moe_router_topk_bf16": ([P, P, I64, I64, I, I, P, P, P], I),
     "remora_b200_moe_dispatch_workspace_bytes": ([I64, I, I], ctypes.c_size_t),
     "remora_b200_moe_dispatch": ([P, I64, I, I, P, P, P, P, P, ctypes.c_size_t, P], I),
+    "remora_b200_moe_dispatch_noalloc": ([P, I64, I, I, P, P, P, P, P], I),
     "remora_b200_moe_gather": ([P, P, I64, I, I64, P, P], I),
     "remora_b200_grouped_gemm_swiglu_bf16": ([P, P, P, P, P, I64, I64, I64, I, P], I),
     "remora_b200_grouped_gemm_bf16": ([P, P, P, P, I64, I64, I64, I, P], I),

@@ -8,4 +8,5 @@
 #include "moe.cu"
 #include "moe_gemm.cu"
 #include "moe_host.cu"
+#include "moe_noalloc.cu"
 #include "dispatch.cu"
