@@ -36,7 +36,7 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # dram__bytes_read.sum + dram__bytes_write.sum per launch of the dominant
 # kernel, from the ncu captures summarised in profiles/ (None = not captured).
 NCU_TRAFFIC_BYTES = {
-    "gemm_8192": None,
+    "gemm_8192": 1140578560,  # profiles/gemm_bf16_8192_dram.md
     "gemm_batched": None,
     "elementwise": None,
 }
@@ -196,6 +196,41 @@ def cpu_baseline_gemm(budget_s: float = 12.0):
                       f"orc_gemm_bf16_rows, gcc -O2 -fopenmp, {threads} threads), {el:.1f} s"}
 
 
+def cpu_baseline_moe(cfg: str, sample_rows: int = 0):
+    """Oracle MoE layer on the host: routing and dispatch of every token, then
+    the SwiGLU expert FFN on a sample of routed rows (all through one
+    expert's weights -- the work per row is the same for every expert) and
+    the combine; tokens/s extrapolated to the whole batch."""
+    import oracle
+
+    c = MOE_CONFIGS[cfg]
+    T, D, F, E, k = c["T"], c["D"], c["F"], c["E"], c["k"]
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    rows = sample_rows or 2 * threads
+    x = oracle.to_bf16(oracle.normal("moe_x", (T, D)))
+    wr = oracle.to_bf16(oracle.normal("moe_router", (D, E), sigma=0.02))
+    wg = oracle.to_bf16(oracle.normal("moe_wg", (D, F), sigma=0.02))
+    wu = oracle.to_bf16(oracle.normal("moe_wu", (D, F), sigma=0.02))
+    wd = oracle.to_bf16(oracle.normal("moe_wd", (F, D), sigma=0.02))
+    t0 = time.perf_counter()
+    idx, w = oracle.router_topk(x, wr, k)
+    _, _, perm, inv = oracle.dispatch(idx, E)
+    t_route = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    _, y, _ = oracle.expert_ffn(x[perm[:rows] // k], wg, wu, wd)
+    t_rows = time.perf_counter() - t0
+    ntok = max(1, rows // k)
+    t0 = time.perf_counter()
+    oracle.combine(y[: ntok * k], np.arange(ntok * k, dtype=np.int32).reshape(-1, k), w[:ntok])
+    t_comb = time.perf_counter() - t0
+    total = t_route + t_rows * (T * k) / rows + t_comb * T / ntok
+    return {"value": T / total, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"router+dispatch of all {T} tokens ({t_route:.2f} s), SwiGLU FFN of "
+                      f"{rows} routed rows ({t_rows:.2f} s), combine of {ntok} tokens; "
+                      f"extrapolated to {T * k} rows; oracle/oracle.c, {threads} threads"}
+
+
 # -------------------------------------------------------------------- GEMM
 def bench_gemm(args, world, rank, local):
     import torch
@@ -204,7 +239,11 @@ def bench_gemm(args, world, rank, local):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    if world == 1:
+    if args.size:
+        batch_local, M, N, K = 1, args.size, args.size, args.size
+        workload = f"dot_general bf16 [{M},{K}]x[{K},{N}] (profiling case)"
+        cfg_key = "gemm_size"
+    elif world == 1:
         batch_local, M, N, K = 1, 8192, 8192, 8192
         workload = "dot_general bf16 [8192,8192]x[8192,8192]->[8192,8192], fp32 accumulate"
         cfg_key = "gemm_8192"
@@ -215,7 +254,7 @@ def bench_gemm(args, world, rank, local):
         workload = (f"dot_general bf16 batched [8,4096,4096]x[8,4096,4096], batch sharded "
                     f"{batch_local} per rank over {world} GPUs")
         cfg_key = "gemm_batched"
-    flop_step = 2.0 * 8192 ** 3  # the whole job's work per step (both forms)
+    flop_step = 2.0 * batch_local * M * N * K * world  # the whole job's work per step
     A = torch.empty(batch_local, M, K, dtype=torch.bfloat16, device=dev)
     B = torch.empty(batch_local, K, N, dtype=torch.bfloat16, device=dev)
     C = torch.empty(batch_local, M, N, dtype=torch.bfloat16, device=dev)
@@ -297,6 +336,123 @@ def bench_gemm(args, world, rank, local):
         "clocks": clk.summary(),
     }
     return line
+
+
+# --------------------------------------------------------------------- MoE
+MOE_CONFIGS = {
+    "4": dict(T=8192, D=4096, F=14336, E=8, k=2),
+    "5": dict(T=65536, D=2048, F=1536, E=64, k=8),
+}
+
+
+def _cuda_time(fn, reps, dev):
+    import torch
+
+    s = torch.cuda.current_stream(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    for _ in range(reps):
+        fn()
+    b.record(s)
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(b) / reps
+
+
+def bench_moe(args, world, rank, local):
+    """The MoE layer (router, dispatch, SwiGLU expert GEMMs, combine) on one
+    GPU per rank; tokens/s = T / layer time."""
+    import torch
+
+    import remora_b200 as rb
+
+    c = MOE_CONFIGS[args.moe_config]
+    T, D, F, E, k = c["T"], c["D"], c["F"], c["E"], c["k"]
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    x = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    wr = torch.empty(D, E, dtype=torch.bfloat16, device=dev)
+    wg = torch.empty(E, D, F, dtype=torch.bfloat16, device=dev)
+    wu = torch.empty(E, D, F, dtype=torch.bfloat16, device=dev)
+    wd = torch.empty(E, F, D, dtype=torch.bfloat16, device=dev)
+    for t, stream_id, sig in ((x, 30, 1.0), (wr, 31, 0.02), (wg, 32, 0.02), (wu, 33, 0.02),
+                              (wd, 34, 0.02)):
+        rb.fill_normal(t, rb.stream_key(stream_id + 100 * rank), 0.0, sig)
+    out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    ws = torch.empty(rb.moe_workspace_bytes(T, D, F, E, k), dtype=torch.uint8, device=dev)
+
+    def step():
+        rb.moe_layer(x, wr, wg, wu, wd, k, out=out, workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    rb.synchronize_and_check(dev)
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    rb.synchronize_and_check(dev)
+
+    # per-kernel times of the expert GEMMs on the same routing (roofline)
+    idx, w = rb.moe_router_topk(x, wr, k)
+    counts, offsets, perm, inv = rb.moe_dispatch(idx, E)
+    xs = rb.moe_gather(x, perm, k)
+    h = rb.grouped_gemm_swiglu(xs, wg, wu, offsets)
+    y = rb.grouped_gemm(h, wd, offsets)
+    reps = 5
+    t_up = _cuda_time(lambda: rb.grouped_gemm_swiglu(xs, wg, wu, offsets), reps, dev)
+    t_down = _cuda_time(lambda: rb.grouped_gemm(h, wd, offsets), reps, dev)
+    t_router = _cuda_time(lambda: rb.moe_router_topk(x, wr, k), reps, dev)
+    rows = T * k
+    flop_up = 2.0 * rows * D * F * 2
+    flop_down = 2.0 * rows * F * D
+    peaks, src = load_peaks()
+    up_tf = flop_up / (t_up * 1e-3) / 1e12
+
+    # end to end: tokens in from pinned host memory, layer output back
+    xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+    oh = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    xh.copy_(x)
+
+    def e2e_step():
+        x.copy_(xh, non_blocking=True)
+        step()
+        oh.copy_(out, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_ms = max_over_ranks(_cuda_time(e2e_step, max(3, min(args.steps, 10)), dev), world)
+    tokens = T * world
+    return {
+        "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, bf16)",
+        "config": {"workload": f"MoE layer config {args.moe_config}: T={T} D={D} F={F} E={E} "
+                               f"top-{k}, SwiGLU experts", "parallelism":
+                   f"independent layer per rank x{world}" if world > 1 else "single GPU",
+                   "expert_flop_per_step": (flop_up + flop_down) * world,
+                   "expert_tflops": (flop_up + flop_down) / (ms * 1e-3) / 1e12,
+                   "kernel_ms": {"grouped_swiglu": t_up, "grouped_down": t_down,
+                                 "router_topk": t_router},
+                   "l2": "weights and activations > 126 MB L2 (no flush)"},
+        "roofline": {"bound": "tensor", "achieved": up_tf, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": up_tf / peaks["bf16_tflops"],
+                     "peak_sustained": peaks.get("bf16_tflops_sustained"), "peak_source": src,
+                     "traffic": NCU_TRAFFIC_BYTES.get("moe_swiglu_" + args.moe_config),
+                     "kernel": "rb::moe::k_grouped_gemm<true>",
+                     "down_tflops": flop_down / (t_down * 1e-3) / 1e12},
+        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": x.numel() * 2 * world,
+                "d2h_bytes_per_step": out.numel() * 2 * world, "ms_per_step": e2e_ms},
+        "gpu_launches": 8 * args.steps, "clocks": clk.summary(),
+    }
 
 
 # ------------------------------------------------------------- elementwise
@@ -388,7 +544,10 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "elementwise"], default="gemm")
+    ap.add_argument("--workload", choices=["gemm", "elementwise", "moe"], default="gemm")
+    ap.add_argument("--moe-config", choices=sorted(MOE_CONFIGS), default="4")
+    ap.add_argument("--size", type=int, default=0,
+                    help="gemm: run an MxNxK = size^3 case instead of the configuration")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -406,10 +565,15 @@ def main():
     from remora_b200 import build
 
     build.build()  # no-op when the in-tree library is current
-    fn = {"gemm": bench_gemm, "elementwise": bench_elementwise}[args.workload]
+    fn = {"gemm": bench_gemm, "elementwise": bench_elementwise, "moe": bench_moe}[args.workload]
     line = fn(args, world, rank, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_gemm() if args.workload == "gemm" else None
+        if args.workload == "gemm":
+            line["cpu_baseline"] = cpu_baseline_gemm()
+        elif args.workload == "moe":
+            line["cpu_baseline"] = cpu_baseline_moe(args.moe_config)
+        else:
+            line["cpu_baseline"] = None
     elif rank == 0:
         line["cpu_baseline"] = None
     if rank == 0:

@@ -21,9 +21,8 @@ namespace moe {
 // top-k indices are bit-identical to it.  A bf16 x bf16 product is exact in
 // fp32, so fmaf(a, b, acc) == acc + a*b here.
 constexpr int kRouterThreads = 256;
-constexpr int kRouterR = 4;   // tokens per thread (independent chains)
-constexpr int kRouterDC = 64; // d per shared-memory chunk
-constexpr int kRowPad = kRouterDC + 8;  // bf16 elements per padded smem row
+constexpr int kRouterDC = 64;           // d per shared-memory chunk
+constexpr int kRowPad = kRouterDC + 8;  // bf16 elements per padded token row
 
 __device__ __forceinline__ bool topk_before(float a, int ia, float b, int ib) {
   const bool an = a != a, bn = b != b;
@@ -32,24 +31,26 @@ __device__ __forceinline__ bool topk_before(float a, int ia, float b, int ib) {
   return ia < ib;
 }
 
-__device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
-
+// G token groups x E experts threads; each thread owns R tokens (R
+// independent chains).  Shared memory per d-chunk: the block's tokens
+// [TPB][kRowPad] and the router chunk in its natural [kRouterDC][E] layout
+// (a warp then reads consecutive experts: no bank conflicts, no transpose).
+template <int R>
 __global__ void __launch_bounds__(kRouterThreads)
     k_router_topk(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr, int T, int D,
                   int E, int k, int G, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
-  // G token groups x E experts threads; each thread owns kRouterR tokens.
   extern __shared__ __align__(16) uint8_t sm_raw[];
-  const int TPB = G * kRouterR;
+  const int TPB = G * R;
   uint16_t* xs = reinterpret_cast<uint16_t*>(sm_raw);                 // [TPB][kRowPad]
-  uint16_t* ws = xs + TPB * kRowPad;                                  // [E][kRowPad]
-  float* lg = reinterpret_cast<float*>(ws + E * kRowPad);             // [TPB][E]
+  uint16_t* ws = xs + TPB * kRowPad;                                  // [kRouterDC][E]
+  float* lg = reinterpret_cast<float*>(ws + ((kRouterDC * E + 7) & ~7));  // [TPB][E]
   const int tid = threadIdx.x;
   const int e = tid % E, g = tid / E;
   const bool active = g < G;
   const int t0 = blockIdx.x * TPB;
-  float acc[kRouterR];
+  float acc[R];
 #pragma unroll
-  for (int r = 0; r < kRouterR; ++r) acc[r] = 0.0f;
+  for (int r = 0; r < R; ++r) acc[r] = 0.0f;
 
   for (int d0 = 0; d0 < D; d0 += kRouterDC) {
     const int dc = min(kRouterDC, D - d0);
@@ -61,27 +62,33 @@ __global__ void __launch_bounds__(kRouterThreads)
         v = *reinterpret_cast<const uint4*>(x + (int64_t)(t0 + row) * D + d0 + c8);
       *reinterpret_cast<uint4*>(xs + row * kRowPad + c8) = v;
     }
-    // router chunk transposed to [E][d]
-    for (int i = tid; i < kRouterDC * E; i += blockDim.x) {
-      const int dd = i / E, ee = i % E;
-      ws[ee * kRowPad + dd] = dd < dc ? wr[(int64_t)(d0 + dd) * E + ee] : (uint16_t)0;
+    // router chunk rows d0 .. d0+dc-1 (contiguous in global memory)
+    if ((E & 7) == 0) {
+      const int n8 = kRouterDC * E / 8;
+      for (int i = tid; i < n8; i += blockDim.x) {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (i * 8 < dc * E) v = *reinterpret_cast<const uint4*>(wr + (int64_t)d0 * E + i * 8);
+        *reinterpret_cast<uint4*>(ws + i * 8) = v;
+      }
+    } else {
+      for (int i = tid; i < kRouterDC * E; i += blockDim.x)
+        ws[i] = i < dc * E ? wr[(int64_t)d0 * E + i] : (uint16_t)0;
     }
     __syncthreads();
     if (active) {
-      const uint16_t* wrow = ws + e * kRowPad;
 #pragma unroll 2
       for (int dd = 0; dd < kRouterDC; dd += 8) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(wrow + dd);
-        const uint32_t wq[4] = {wv.x, wv.y, wv.z, wv.w};
+        float wv[8];
 #pragma unroll
-        for (int r = 0; r < kRouterR; ++r) {
-          const uint4 xv = *reinterpret_cast<const uint4*>(xs + (g * kRouterR + r) * kRowPad + dd);
+        for (int q = 0; q < 8; ++q) wv[q] = __uint_as_float((uint32_t)ws[(dd + q) * E + e] << 16);
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const uint4 xv = *reinterpret_cast<const uint4*>(xs + (g * R + r) * kRowPad + dd);
           const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
-            acc[r] = fmaf(__uint_as_float(xq[q] << 16), __uint_as_float(wq[q] << 16), acc[r]);
-            acc[r] = fmaf(__uint_as_float(xq[q] & 0xffff0000u),
-                          __uint_as_float(wq[q] & 0xffff0000u), acc[r]);
+            acc[r] = fmaf(__uint_as_float(xq[q] << 16), wv[2 * q], acc[r]);
+            acc[r] = fmaf(__uint_as_float(xq[q] & 0xffff0000u), wv[2 * q + 1], acc[r]);
           }
         }
       }
@@ -90,7 +97,7 @@ __global__ void __launch_bounds__(kRouterThreads)
   }
   if (active) {
 #pragma unroll
-    for (int r = 0; r < kRouterR; ++r) lg[(g * kRouterR + r) * E + e] = acc[r];
+    for (int r = 0; r < R; ++r) lg[(g * R + r) * E + e] = acc[r];
   }
   __syncthreads();
 

@@ -22,16 +22,23 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
   int G = kRouterThreads / E;
   if (G > 32) G = 32;
   if (G < 1) G = 1;
+  const int R = E <= 16 ? 4 : (E <= 32 ? 8 : 16);  // tokens per thread: 64-128 per block
   const int threads = ((G * E + 31) / 32) * 32;
-  const int TPB = G * kRouterR;
-  const size_t smem = (size_t)(TPB + E) * kRowPad * 2 + (size_t)TPB * E * 4;
-  if (smem > 48 * 1024)
-    RB_CUDA(cudaFuncSetAttribute(k_router_topk, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)smem));
+  const int TPB = G * R;
+  const size_t smem = (size_t)TPB * kRowPad * 2 + (size_t)((kRouterDC * E + 7) & ~7) * 2 +
+                      (size_t)TPB * E * 4;
   const int64_t grid = (T + TPB - 1) / TPB;
-  k_router_topk<<<(unsigned)grid, threads, smem, st>>>(
-      static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(wr), (int)T, (int)D, E, k, G,
-      idx, w);
+  auto launch = [&](auto kern) -> int {
+    if (smem > 48 * 1024)
+      RB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<(unsigned)grid, threads, smem, st>>>(static_cast<const uint16_t*>(x),
+                                               static_cast<const uint16_t*>(wr), (int)T, (int)D,
+                                               E, k, G, idx, w);
+    return REMORA_B200_OK;
+  };
+  int rc = R == 4 ? launch(k_router_topk<4>) : R == 8 ? launch(k_router_topk<8>)
+                                                     : launch(k_router_topk<16>);
+  if (rc) return rc;
   RB_LAUNCH_CHECK();
   return REMORA_B200_OK;
 }
