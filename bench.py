@@ -455,6 +455,94 @@ def bench_moe(args, world, rank, local):
     }
 
 
+def bench_moe_ep(args, world, rank, local):
+    """Expert-parallel MoE, config 5: 65536 tokens split over the ranks,
+    64 experts split over the ranks (8 per GPU at 8 GPUs), token dispatch
+    and combine by NCCL all-to-all.  One GPU runs the single-GPU layer."""
+    import torch
+
+    import remora_b200 as rb
+    from remora_b200.ep import moe_ep_forward
+
+    c = MOE_CONFIGS["5"]
+    T, D, F, E, k = c["T"], c["D"], c["F"], c["E"], c["k"]
+    if T % world or E % world:
+        raise SystemExit(f"config 5 does not split over {world} ranks")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    tl, Epr = T // world, E // world
+    x = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    wr = torch.empty(D, E, dtype=torch.bfloat16, device=dev)
+    rb.fill_normal(x, rb.stream_key(30), 0.0, 1.0)
+    rb.fill_normal(wr, rb.stream_key(31), 0.0, 0.02)
+    x = x[rank * tl:(rank + 1) * tl].contiguous()
+    ws = []
+    for sid, shape in ((32, (E, D, F)), (33, (E, D, F)), (34, (E, F, D))):
+        full = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+        rb.fill_normal(full, rb.stream_key(sid), 0.0, 0.02)
+        ws.append(full if world == 1 else full[rank * Epr:(rank + 1) * Epr].contiguous())
+        del full
+    wg, wu, wd = ws
+    out = torch.empty(tl, D, dtype=torch.bfloat16, device=dev)
+    lws = (torch.empty(rb.moe_workspace_bytes(T, D, F, E, k), dtype=torch.uint8, device=dev)
+           if world == 1 else None)
+
+    def step():
+        if world == 1:
+            rb.moe_layer(x, wr, wg, wu, wd, k, out=out, workspace=lws)
+        else:
+            out.copy_(moe_ep_forward(x, wr, wg, wu, wd, k, E))
+
+    for _ in range(args.warmup):
+        step()
+    rb.synchronize_and_check(dev)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
+    oh = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    xh.copy_(x)
+
+    def e2e_step():
+        x.copy_(xh, non_blocking=True)
+        step()
+        oh.copy_(out, non_blocking=True)
+
+    e2e_step()
+    barrier(world)
+    e2e_ms = max_over_ranks(_cuda_time(e2e_step, max(3, min(args.steps, 10)), dev), world)
+    flop = 6.0 * D * F * T * k
+    peaks, src = load_peaks()
+    per_gpu_tf = flop / world / (ms * 1e-3) / 1e12
+    return {
+        "metric": METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, bf16)",
+        "config": {"workload": f"expert-parallel MoE config 5: T={T} D={D} F={F} E={E} top-{k}, "
+                               f"{Epr} experts and {tl} tokens per GPU",
+                   "parallelism": f"EP{world} (NCCL all-to-all)" if world > 1 else "single GPU",
+                   "expert_flop_per_step": flop},
+        "roofline": {"bound": "tensor", "achieved": per_gpu_tf, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": per_gpu_tf / peaks["bf16_tflops"],
+                     "peak_source": src, "traffic": None,
+                     "kernel": "whole layer per GPU (expert FLOP / layer time)"},
+        "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": x.numel() * 2 * world,
+                "d2h_bytes_per_step": out.numel() * 2 * world, "ms_per_step": e2e_ms},
+        "gpu_launches": 8 * args.steps, "clocks": clk.summary(),
+    }
+
+
 # ------------------------------------------------------------- elementwise
 def bench_elementwise(args, world, rank, local):
     """scale -> add -> exp chain: the named [1,8,128,128] shape (latency
@@ -544,7 +632,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "elementwise", "moe"], default="gemm")
+    ap.add_argument("--workload", choices=["gemm", "elementwise", "moe", "moe_ep"],
+                    default="gemm")
     ap.add_argument("--moe-config", choices=sorted(MOE_CONFIGS), default="4")
     ap.add_argument("--size", type=int, default=0,
                     help="gemm: run an MxNxK = size^3 case instead of the configuration")
@@ -565,7 +654,8 @@ def main():
     from remora_b200 import build
 
     build.build()  # no-op when the in-tree library is current
-    fn = {"gemm": bench_gemm, "elementwise": bench_elementwise, "moe": bench_moe}[args.workload]
+    fn = {"gemm": bench_gemm, "elementwise": bench_elementwise, "moe": bench_moe,
+          "moe_ep": bench_moe_ep}[args.workload]
     line = fn(args, world, rank, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         if args.workload == "gemm":

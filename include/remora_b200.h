@@ -217,6 +217,21 @@ int remora_b200_grouped_gemm_swiglu_bf16(const void* xs, const void* wg, const v
 int remora_b200_grouped_gemm_bf16(const void* a, const void* w, void* y, const int32_t* offsets,
                                   int64_t rows, int64_t K, int64_t N, int E, void* stream);
 
+/* The two grouped GEMMs over row segments that name their expert: segment q
+ * owns rows [seg_offsets[q], seg_offsets[q+1]) and uses expert
+ * seg_expert[q] (0 <= seg_expert[q] < E, n_seg <= 256).  This is the layout
+ * of the rows an expert-parallel rank receives from its peers: ordered by
+ * source rank, then by local expert.  Same arithmetic as the forms above. */
+int remora_b200_grouped_gemm_swiglu_segments_bf16(const void* xs, const void* wg, const void* wu,
+                                                  void* h, const int32_t* seg_offsets,
+                                                  const int32_t* seg_expert, int n_seg,
+                                                  int64_t rows, int64_t D, int64_t F, int E,
+                                                  void* stream);
+int remora_b200_grouped_gemm_segments_bf16(const void* a, const void* w, void* y,
+                                           const int32_t* seg_offsets, const int32_t* seg_expert,
+                                           int n_seg, int64_t rows, int64_t K, int64_t N, int E,
+                                           void* stream);
+
 /* Combine (mixtral_moe_layer.mlir:43-46, :52-55): out[t, :] =
  * bf16(0 + w[t,0]*y[inv[t,0]] + w[t,1]*y[inv[t,1]] + ...), slot order, each
  * product and sum rounded separately.  y bf16 [T*k, D]; out bf16 [T, D]. */

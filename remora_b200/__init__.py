@@ -75,6 +75,9 @@ _SIGNATURES = {
     "remora_b200_moe_gather": ([P, P, I64, I, I64, P, P], I),
     "remora_b200_grouped_gemm_swiglu_bf16": ([P, P, P, P, P, I64, I64, I64, I, P], I),
     "remora_b200_grouped_gemm_bf16": ([P, P, P, P, I64, I64, I64, I, P], I),
+    "remora_b200_grouped_gemm_swiglu_segments_bf16": ([P, P, P, P, P, P, I, I64, I64, I64, I, P],
+                                                      I),
+    "remora_b200_grouped_gemm_segments_bf16": ([P, P, P, P, P, I, I64, I64, I64, I, P], I),
     "remora_b200_moe_combine_bf16": ([P, P, P, I64, I, I64, P, P], I),
     "remora_b200_moe_workspace_bytes": ([I64, I64, I64, I, I], ctypes.c_size_t),
     "remora_b200_moe_layer_bf16": ([P, P, P, P, P, P, I64, I64, I64, I, I, P, ctypes.c_size_t, P],
@@ -315,6 +318,35 @@ def grouped_gemm(a: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor) -> tor
     _check(lib().remora_b200_grouped_gemm_bf16(a.contiguous().data_ptr(), w.contiguous().data_ptr(),
                                                y.data_ptr(), offsets.data_ptr(), rows, K, N, E,
                                                _stream(a)))
+    return y
+
+
+def grouped_gemm_swiglu_segments(xs, wg, wu, seg_offsets, seg_expert) -> torch.Tensor:
+    """SwiGLU grouped GEMM over row segments that name their expert."""
+    _dev(xs, wg, wu, seg_offsets, seg_expert)
+    _bf16(xs, wg, wu)
+    _i32(seg_offsets, seg_expert)
+    rows, D = xs.shape
+    E, _, F = wg.shape
+    h = torch.empty((rows, F), dtype=torch.bfloat16, device=xs.device)
+    _check(lib().remora_b200_grouped_gemm_swiglu_segments_bf16(
+        xs.contiguous().data_ptr(), wg.contiguous().data_ptr(), wu.contiguous().data_ptr(),
+        h.data_ptr(), seg_offsets.data_ptr(), seg_expert.data_ptr(), seg_expert.numel(), rows, D,
+        F, E, _stream(xs)))
+    return h
+
+
+def grouped_gemm_segments(a, w, seg_offsets, seg_expert) -> torch.Tensor:
+    """Grouped GEMM over row segments that name their expert (w [E, K, N])."""
+    _dev(a, w, seg_offsets, seg_expert)
+    _bf16(a, w)
+    _i32(seg_offsets, seg_expert)
+    rows, K = a.shape
+    E, _, N = w.shape
+    y = torch.empty((rows, N), dtype=torch.bfloat16, device=a.device)
+    _check(lib().remora_b200_grouped_gemm_segments_bf16(
+        a.contiguous().data_ptr(), w.contiguous().data_ptr(), y.data_ptr(), seg_offsets.data_ptr(),
+        seg_expert.data_ptr(), seg_expert.numel(), rows, K, N, E, _stream(a)))
     return y
 
 

@@ -28,14 +28,16 @@ constexpr uint32_t GABytes = GBM * GBK * 2;        // 16 KB
 constexpr uint32_t GBBytes = 256 * GBK * 2;        // 32 KB: 4 boxes of [64 K x 64 N]
 constexpr uint32_t GStageBytes = GABytes + GBBytes;
 constexpr uint32_t GBarOffset = GStages * GStageBytes;
-constexpr uint32_t GSmemBytes = GBarOffset + 256 + 2 * (GMaxE + 1) * 4 + 1024;
+constexpr uint32_t GSmemBytes = GBarOffset + 256 + 3 * (GMaxE + 1) * 4 + 1024;
 
 struct GroupShape {
   int K, N, E;
+  int S;             // row segments (== E when segments are the experts)
   int tiles_n;       // N / (columns per tile)
   int num_kb;
-  const int32_t* offsets;  // [E+1] device: expert row segments
-  uint16_t* out;           // [rows, N] bf16
+  const int32_t* offsets;     // [S+1] device: row segments
+  const int32_t* seg_expert;  // [S] device: expert of each segment, or null (segment s = expert s)
+  uint16_t* out;              // [rows, N] bf16
 };
 
 struct GSmem {
@@ -52,7 +54,7 @@ struct TileInfo {
 };
 
 __device__ __forceinline__ TileInfo group_tile(const GroupShape& s, const int* mt, const int* off,
-                                               int total_mt, int t) {
+                                               const int* sexp, int total_mt, int t) {
   const int span = GGroupM * s.tiles_n;
   const int grp = t / span;
   const int first = grp * GGroupM;
@@ -61,12 +63,12 @@ __device__ __forceinline__ TileInfo group_tile(const GroupShape& s, const int* m
   const int g = first + rr % gm;
   TileInfo ti;
   ti.n = rr / gm;
-  int lo = 0, hi = s.E;  // last e with mt[e] <= g
+  int lo = 0, hi = s.S;  // last segment with mt[seg] <= g
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
     if (mt[mid] <= g) lo = mid; else hi = mid;
   }
-  ti.e = lo;
+  ti.e = sexp[lo];
   ti.r0 = off[lo] + (g - mt[lo]) * GBM;
   ti.r_end = off[lo + 1];
   return ti;
@@ -88,18 +90,26 @@ __global__ void __launch_bounds__(GThreads, 1)
   GSmem* sm = reinterpret_cast<GSmem*>(smem + GBarOffset);
   int* s_mt = reinterpret_cast<int*>(smem + GBarOffset + 256);
   int* s_off = s_mt + (GMaxE + 1);
+  int* s_exp = s_off + (GMaxE + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  for (int i = threadIdx.x; i <= s.E; i += blockDim.x) s_off[i] = s.offsets[i];
+  for (int i = threadIdx.x; i <= s.S; i += blockDim.x) {
+    s_off[i] = s.offsets[i];
+    if (i < s.S) {
+      const int e = s.seg_expert ? s.seg_expert[i] : i;
+      s_exp[i] = (e >= 0 && e < s.E) ? e : 0;
+      if (e < 0 || e >= s.E) atomicExch(&g_device_error, 2);
+    }
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
-    // m-tile prefix: expert e owns tiles [s_mt[e], s_mt[e+1]) of GBM rows
+    // m-tile prefix: segment q owns tiles [s_mt[q], s_mt[q+1]) of GBM rows
     int mt = 0;
-    for (int e = 0; e < s.E; ++e) {
-      s_mt[e] = mt;
-      mt += (s_off[e + 1] - s_off[e] + GBM - 1) / GBM;
+    for (int q = 0; q < s.S; ++q) {
+      s_mt[q] = mt;
+      mt += (s_off[q + 1] - s_off[q] + GBM - 1) / GBM;
     }
-    s_mt[s.E] = mt;
+    s_mt[s.S] = mt;
     for (int i = 0; i < GStages; ++i) {
       mbar_init(&sm->full[i], 1);
       mbar_init(&sm->empty[i], 1);
@@ -121,7 +131,7 @@ __global__ void __launch_bounds__(GThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = sm->tmem_base;
   volatile int* abort_flag = &sm->abort_flag;
-  const int total_mt = s_mt[s.E];
+  const int total_mt = s_mt[s.S];
   const int total_tiles = total_mt * s.tiles_n;
   constexpr int kColsPerTile = kSwiGLU ? 128 : 256;
 
@@ -133,7 +143,7 @@ __global__ void __launch_bounds__(GThreads, 1)
       int stage = 0, issued = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
-        const TileInfo ti = group_tile(s, s_mt, s_off, total_mt, t);
+        const TileInfo ti = group_tile(s, s_mt, s_off, s_exp, total_mt, t);
         const int n0 = ti.n * kColsPerTile;
         for (int kb = 0; kb < s.num_kb; ++kb) {
           if (!mbar_wait(&sm->empty[stage], phase ^ 1)) { *abort_flag = 1; break; }
@@ -210,7 +220,7 @@ __global__ void __launch_bounds__(GThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const TileInfo ti = group_tile(s, s_mt, s_off, total_mt, t);
+      const TileInfo ti = group_tile(s, s_mt, s_off, s_exp, total_mt, t);
       bool got = !*abort_flag && mbar_wait(&sm->tmem_full[acc], acc_phase);
       if (!__all_sync(0xffffffffu, got)) { *abort_flag = 1; break; }
       tc_fence_after();

@@ -87,9 +87,11 @@ int gather_launch(const void* x, const int32_t* perm, int64_t rows, int k, int64
 // SwiGLU form) [E, K, N]; out [rows, N].  offsets [E+1] on the device.
 int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, void* out,
                    const int32_t* offsets, int64_t rows, int64_t K, int64_t N, int E,
-                   cudaStream_t st) {
+                   cudaStream_t st, const int32_t* seg_expert = nullptr, int n_seg = -1) {
   const int cols = swiglu ? 128 : 256;
+  const int S = n_seg < 0 ? E : n_seg;
   RB_CHECK_ARG(E >= 1 && E <= GMaxE, "grouped_gemm: E=%d unsupported (1..%d)", E, GMaxE);
+  RB_CHECK_ARG(S >= 1 && S <= GMaxE, "grouped_gemm: %d segments unsupported (1..%d)", S, GMaxE);
   RB_CHECK_ARG(rows >= 0 && K > 0 && N > 0 && K % 8 == 0 && N % cols == 0,
                "grouped_gemm: need K %% 8 == 0 and N %% %d == 0 (K=%lld N=%lld)", cols,
                (long long)K, (long long)N);
@@ -122,12 +124,14 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   sh.K = (int)K;
   sh.N = (int)N;
   sh.E = E;
+  sh.S = S;
+  sh.seg_expert = seg_expert;
   sh.tiles_n = (int)(N / cols);
   sh.num_kb = (int)((K + GBK - 1) / GBK);
   sh.offsets = offsets;
   sh.out = static_cast<uint16_t*>(out);
   // upper bound of the tile count: sum over experts of ceil(n_e / 128)
-  const int64_t max_tiles = (rows / GBM + E) * (int64_t)sh.tiles_n;
+  const int64_t max_tiles = (rows / GBM + S) * (int64_t)sh.tiles_n;
   int grid = num_sms();
   if (grid > max_tiles) grid = (int)max_tiles;
   if (swiglu) {
@@ -239,6 +243,27 @@ extern "C" int remora_b200_grouped_gemm_bf16(const void* a, const void* w, void*
                                              int64_t N, int E, void* stream) {
   clear_error();
   return grouped_launch(false, a, w, nullptr, y, offsets, rows, K, N, E, as_stream(stream));
+}
+
+extern "C" int remora_b200_grouped_gemm_swiglu_segments_bf16(
+    const void* xs, const void* wg, const void* wu, void* h, const int32_t* seg_offsets,
+    const int32_t* seg_expert, int n_seg, int64_t rows, int64_t D, int64_t F, int E,
+    void* stream) {
+  clear_error();
+  RB_CHECK_ARG(seg_expert, "grouped_gemm_segments: null seg_expert");
+  return grouped_launch(true, xs, wg, wu, h, seg_offsets, rows, D, F, E, as_stream(stream),
+                        seg_expert, n_seg);
+}
+
+extern "C" int remora_b200_grouped_gemm_segments_bf16(const void* a, const void* w, void* y,
+                                                      const int32_t* seg_offsets,
+                                                      const int32_t* seg_expert, int n_seg,
+                                                      int64_t rows, int64_t K, int64_t N, int E,
+                                                      void* stream) {
+  clear_error();
+  RB_CHECK_ARG(seg_expert, "grouped_gemm_segments: null seg_expert");
+  return grouped_launch(false, a, w, nullptr, y, seg_offsets, rows, K, N, E, as_stream(stream),
+                        seg_expert, n_seg);
 }
 
 extern "C" int remora_b200_moe_combine_bf16(const void* y, const int32_t* inv, const float* w,

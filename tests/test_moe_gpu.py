@@ -187,3 +187,29 @@ def test_moe_layer_config4_sampled(rb, orc):
     ref = orc.combine(ysel, np.arange(16 * k, dtype=np.int32).reshape(16, k), rw[toks])
     got = orc.bf16_to_f32(to_np_bf16(out)[toks])
     assert norm_err(got, orc.bf16_to_f32(ref)) <= TOL
+
+
+def test_grouped_gemm_segments_match_expert_order(rb, orc):
+    """Rows regrouped as (source rank, local expert) segments, the layout an
+    expert-parallel rank receives, give the same rows bit for bit."""
+    T, D, F, E, k, P = 600, 256, 256, 8, 2, 3
+    x, wr, wg, wu, wd = _moe_inputs(orc, T, D, F, E)
+    idx, w, counts, offsets, perm, inv, xs = _expert_rows(orc, x, wr, k, E)
+    off_t = torch.from_numpy(offsets).cuda()
+    Xs, Wg, Wu, Wd = (from_np_bf16(a) for a in (xs, wg, wu, wd))
+    y_ref = to_np_bf16(rb.grouped_gemm(rb.grouped_gemm_swiglu(Xs, Wg, Wu, off_t), Wd, off_t))
+    # split each expert's rows into P chunks ("sources"), order source-major
+    order, seg_off, seg_exp = [], [0], []
+    for src in range(P):
+        for e in range(E):
+            a, b = offsets[e], offsets[e + 1]
+            chunk = np.arange(a, b)[src::P]
+            order.extend(chunk.tolist())
+            seg_off.append(seg_off[-1] + len(chunk))
+            seg_exp.append(e)
+    order = np.array(order)
+    so = torch.tensor(seg_off, dtype=torch.int32, device="cuda")
+    se = torch.tensor(seg_exp, dtype=torch.int32, device="cuda")
+    h = rb.grouped_gemm_swiglu_segments(from_np_bf16(xs[order]), Wg, Wu, so, se)
+    y = to_np_bf16(rb.grouped_gemm_segments(h, Wd, so, se))
+    assert np.array_equal(y, y_ref[order])
