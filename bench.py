@@ -491,7 +491,7 @@ def bench_moe_ep(args, world, rank, local):
         if world == 1:
             rb.moe_layer(x, wr, wg, wu, wd, k, out=out, workspace=lws)
         else:
-            out.copy_(moe_ep_forward(x, wr, wg, wu, wd, k, E))
+            out.copy_(moe_ep_forward(x, wr, wg, wu, wd, k, E, chunks=args.ep_chunks or None))
 
     for _ in range(args.warmup):
         step()
@@ -531,6 +531,7 @@ def bench_moe_ep(args, world, rank, local):
         "config": {"workload": f"expert-parallel MoE config 5: T={T} D={D} F={F} E={E} top-{k}, "
                                f"{Epr} experts and {tl} tokens per GPU",
                    "parallelism": f"EP{world} (NCCL all-to-all)" if world > 1 else "single GPU",
+                   "ep_chunks": args.ep_chunks or "default",
                    "expert_flop_per_step": flop},
         "roofline": {"bound": "tensor", "achieved": per_gpu_tf, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": per_gpu_tf / peaks["bf16_tflops"],
@@ -635,6 +636,8 @@ def main():
     ap.add_argument("--workload", choices=["gemm", "elementwise", "moe", "moe_ep"],
                     default="gemm")
     ap.add_argument("--moe-config", choices=sorted(MOE_CONFIGS), default="4")
+    ap.add_argument("--ep-chunks", type=int, default=0,
+                    help="moe_ep: token pieces per layer for comm/compute overlap (0 = default)")
     ap.add_argument("--size", type=int, default=0,
                     help="gemm: run an MxNxK = size^3 case instead of the configuration")
     ap.add_argument("--no-cpu-baseline", action="store_true")

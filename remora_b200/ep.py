@@ -20,9 +20,8 @@ weights, so the result is bit-identical to the single-GPU layer
 
 The local compute goes through an ``ops`` object (``GpuOps`` here: the
 CUDA library; tests substitute CPU restatements to check the exchange
-bookkeeping on gloo ranks).  The row counts are read on the host: NCCL's
-all-to-all-v takes host split sizes, so a layer has two small
-device-to-host reads.
+bookkeeping on gloo ranks).  The row counts are read on the host once per
+layer: NCCL's all-to-all-v takes host split sizes.
 """
 from __future__ import annotations
 
@@ -65,12 +64,20 @@ def segments(recv_counts: torch.Tensor, P: int, Epr: int):
     return offs.to(torch.int32), exp
 
 
-def moe_ep_forward(x, wr, wg_local, wu_local, wd_local, k: int, E: int, group=None, ops=None):
+def moe_ep_forward(x, wr, wg_local, wu_local, wd_local, k: int, E: int, group=None, ops=None,
+                   chunks: int | None = None):
     """One expert-parallel MoE layer on this rank.
 
     x [T_local, D] (this rank's tokens), wr [D, E] (replicated),
     wg_local / wu_local [E/P, D, F], wd_local [E/P, F, D] (this rank's
     experts).  Returns out [T_local, D] bf16.
+
+    With ``chunks`` > 1 the local tokens are processed in pieces: all
+    pieces' counts travel in one all-to-all (one host read), then piece
+    c+1's rows are exchanged while piece c's expert GEMMs run, and piece c's
+    outputs travel back while piece c+1 computes.  Measured on 8 B200s
+    (config 5) one piece is faster: NCCL's kernels and the persistent expert
+    GEMM then compete for SMs, so the default is 1.
     """
     ops = ops or GpuOps()
     P = dist.get_world_size(group)
@@ -80,33 +87,54 @@ def moe_ep_forward(x, wr, wg_local, wu_local, wd_local, k: int, E: int, group=No
     if wg_local.shape[0] != Epr:
         raise ValueError(f"rank holds {wg_local.shape[0]} experts, expected {Epr}")
     T, D = x.shape
-    idx, w = ops.router(x, wr, k)
-    counts, offsets, perm, inv = ops.dispatch(idx, E)
-    xs = ops.gather(x, perm, k)
+    C = chunks or 1
+    C = max(1, min(C, T)) if T else 1
+    pieces = torch.tensor_split(torch.arange(T), C) if T else [torch.arange(0)]
 
-    # 3. counts: rank r sends counts[q*Epr:(q+1)*Epr] to rank q
-    recv_counts = torch.empty_like(counts)
-    dist.all_to_all_single(recv_counts, counts, group=group)
-    send_splits = counts.view(P, Epr).sum(1).tolist()
-    recv_rows = recv_counts.view(P, Epr).sum(1)
-    recv_splits = recv_rows.tolist()
+    # 1-2. local routing, dispatch by global expert, gather, per piece
+    loc = []
+    for pc in pieces:
+        xt = x[int(pc[0]):int(pc[-1]) + 1] if pc.numel() else x[:0]
+        idx, w = ops.router(xt, wr, k)
+        counts, offsets, perm, inv = ops.dispatch(idx, E)
+        loc.append((ops.gather(xt, perm, k), counts, inv, w))
 
-    # 4. rows
-    xr = torch.empty((sum(recv_splits), D), dtype=xs.dtype, device=xs.device)
-    dist.all_to_all_single(xr, xs, output_split_sizes=recv_splits,
-                           input_split_sizes=send_splits, group=group)
+    # 3. every piece's counts in one all-to-all: send [P][C][Epr], recv [P(src)][C][Epr]
+    send_c = torch.stack([l[1] for l in loc]).view(C, P, Epr).transpose(0, 1).contiguous()
+    recv_c = torch.empty_like(send_c)
+    dist.all_to_all_single(recv_c, send_c, group=group)
+    send_rows = send_c.sum(2).t().tolist()        # [C][P]: rows this rank sends
+    recv_rows = recv_c.sum(2).t().tolist()        # [C][P]: rows this rank receives
 
-    # 5. local experts over (source, local expert) segments
-    seg_offsets, seg_expert = segments(recv_counts, P, Epr)
-    if xr.shape[0]:
-        yr = ops.experts(xr, wg_local, wu_local, wd_local, seg_offsets, seg_expert)
-    else:
-        yr = torch.empty((0, D), dtype=xs.dtype, device=xs.device)
+    def rows_exchange(c):
+        xs = loc[c][0]
+        xr = torch.empty((sum(recv_rows[c]), D), dtype=xs.dtype, device=xs.device)
+        work = dist.all_to_all_single(xr, xs, output_split_sizes=recv_rows[c],
+                                      input_split_sizes=send_rows[c], group=group, async_op=True)
+        return xr, work
 
-    # 6. outputs back to the token owners, in the order they were sent
-    y = torch.empty_like(xs)
-    dist.all_to_all_single(y, yr, output_split_sizes=send_splits,
-                           input_split_sizes=recv_splits, group=group)
+    # 4-6. pipeline: rows of c+1 in flight while the experts of c run
+    pending = rows_exchange(0)
+    backs = []
+    for c in range(C):
+        xr, work = pending
+        work.wait()
+        if c + 1 < C:
+            pending = rows_exchange(c + 1)
+        seg_offsets, seg_expert = segments(recv_c[:, c, :].contiguous(), P, Epr)
+        if xr.shape[0]:
+            yr = ops.experts(xr, wg_local, wu_local, wd_local, seg_offsets, seg_expert)
+        else:
+            yr = torch.empty((0, D), dtype=xr.dtype, device=xr.device)
+        y = torch.empty_like(loc[c][0])
+        wb = dist.all_to_all_single(y, yr, output_split_sizes=send_rows[c],
+                                    input_split_sizes=recv_rows[c], group=group, async_op=True)
+        backs.append((y, wb, yr))
 
-    # 7. combine
-    return ops.combine(y, inv, w)
+    # 7. combine each piece in slot order
+    outs = []
+    for c in range(C):
+        y, wb, _ = backs[c]
+        wb.wait()
+        outs.append(ops.combine(y, loc[c][2], loc[c][3]))
+    return torch.cat(outs) if C > 1 else outs[0]
