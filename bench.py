@@ -406,9 +406,9 @@ def bench_moe(args, world, rank, local):
     h = rb.grouped_gemm_swiglu(xs, wg, wu, offsets)
     y = rb.grouped_gemm(h, wd, offsets)
     reps = 5
-    t_up = _cuda_time(lambda: rb.grouped_gemm_swiglu(xs, wg, wu, offsets), reps, dev)
-    t_down = _cuda_time(lambda: rb.grouped_gemm(h, wd, offsets), reps, dev)
-    t_router = _cuda_time(lambda: rb.moe_router_topk(x, wr, k), reps, dev)
+    t_up = _cuda_time(lambda: rb.grouped_gemm_swiglu(xs, wg, wu, offsets, out=h), reps, dev)
+    t_down = _cuda_time(lambda: rb.grouped_gemm(h, wd, offsets, out=y), reps, dev)
+    t_router = _cuda_time(lambda: rb.moe_router_topk(x, wr, k, idx=idx, w=w), reps, dev)
     rows = T * k
     flop_up = 2.0 * rows * D * F * 2
     flop_down = 2.0 * rows * F * D
@@ -544,6 +544,77 @@ def bench_moe_ep(args, world, rank, local):
     }
 
 
+def bench_attention(args, world, rank, local):
+    """Causal softmax attention, Q, K, V bf16 [4, 32, 4096, 128]; the 128
+    (batch, head) pairs are split over the ranks (no collective)."""
+    import torch
+
+    import remora_b200 as rb
+
+    B, H, S, Dh = 4, 32, 4096, 128
+    if (B * H) % world:
+        raise SystemExit(f"{B * H} (batch, head) pairs do not split over {world} ranks")
+    bh = B * H // world
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    q, k, v = (torch.empty(1, bh, S, Dh, dtype=torch.bfloat16, device=dev) for _ in range(3))
+    for t, sid in ((q, 20), (k, 21), (v, 22)):
+        rb.fill_normal(t, rb.stream_key(sid + 100 * rank))
+    o = torch.empty_like(q)
+
+    def step():
+        rb.attention(q, k, v, causal=True, out=o)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    stream = torch.cuda.current_stream(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step()
+        ev1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    ms = max_over_ranks(ms_local, world)
+    flop = 4.0 * B * H * S * S * Dh / 2.0
+    qh, kh, vh, oh = (torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (q, k, v, o))
+    qh.copy_(q), kh.copy_(k), vh.copy_(v)
+
+    def e2e_step():
+        q.copy_(qh, non_blocking=True)
+        k.copy_(kh, non_blocking=True)
+        v.copy_(vh, non_blocking=True)
+        step()
+        oh.copy_(o, non_blocking=True)
+
+    e2e_step()
+    barrier(world)
+    e2e_ms = max_over_ranks(_cuda_time(e2e_step, max(3, min(args.steps, 10)), dev), world)
+    peaks, src = load_peaks()
+    achieved = flop / world / (ms_local * 1e-3) / 1e12
+    return {
+        "metric": METRIC, "value": flop / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16)",
+        "config": {"workload": f"causal attention bf16 [{B},{H},{S},{Dh}], {bh} (batch, head) "
+                               f"pairs per GPU", "flop_convention": "4*B*H*S^2*Dh/2 (causal half)",
+                   "parallelism": f"batch x heads sharded x{world}" if world > 1 else "single GPU",
+                   "l2": "q, k, v 402 MB > 126 MB L2 (no flush)"},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                     "peak_source": src, "traffic": None, "kernel": "rb::attn::k_attention_fwd"},
+        "e2e": {"value": flop / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 3 * q.numel() * 2 * world,
+                "d2h_bytes_per_step": o.numel() * 2 * world, "ms_per_step": e2e_ms},
+        "gpu_launches": args.steps, "clocks": clk.summary(),
+    }
+
+
 # ------------------------------------------------------------- elementwise
 def bench_elementwise(args, world, rank, local):
     """scale -> add -> exp chain: the named [1,8,128,128] shape (latency
@@ -633,7 +704,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "elementwise", "moe", "moe_ep"],
+    ap.add_argument("--workload", choices=["gemm", "elementwise", "moe", "moe_ep", "attention"],
                     default="gemm")
     ap.add_argument("--moe-config", choices=sorted(MOE_CONFIGS), default="4")
     ap.add_argument("--ep-chunks", type=int, default=0,
@@ -658,7 +729,7 @@ def main():
 
     build.build()  # no-op when the in-tree library is current
     fn = {"gemm": bench_gemm, "elementwise": bench_elementwise, "moe": bench_moe,
-          "moe_ep": bench_moe_ep}[args.workload]
+          "moe_ep": bench_moe_ep, "attention": bench_attention}[args.workload]
     line = fn(args, world, rank, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         if args.workload == "gemm":

@@ -85,7 +85,9 @@ typedef struct remora_b200_report {
 
 /* 1 if `test` (the --test= kind) is handled by this library, else 0.
  * Kinds: "elementwise" (gpu_tests.cpp:35-95), "projection"
- * (cpu_tests.cpp:65-97), "elementwise_chain", "gemm", "attention". */
+ * (cpu_tests.cpp:65-97), "elementwise_chain", "gemm", "attention", "moe"
+ * (configs "4", "5", "mixtral" = mixtral_moe_layer.mlir:8, "simple" =
+ * simple_moe.mlir:16, with bf16 operands). */
 int remora_b200_recognise(const char* test);
 
 /* Runs the recognised program end to end on `o->device`: allocates its own
@@ -206,14 +208,14 @@ int remora_b200_moe_gather(const void* x, const int32_t* perm, int64_t rows, int
  * for rows r of expert e (offsets[e] <= r < offsets[e+1]),
  * h[r, :] = silu(xs[r] . wg[e]) * (xs[r] . wu[e]), silu(g) = g / (1 + exp(-g)).
  * xs bf16 [rows, D]; wg, wu bf16 [E, D, F]; h bf16 [rows, F].
- * D % 8 == 0, F % 128 == 0; offsets on the device. */
+ * D % 8 == 0, F % 32 == 0; offsets on the device. */
 int remora_b200_grouped_gemm_swiglu_bf16(const void* xs, const void* wg, const void* wu, void* h,
                                          const int32_t* offsets, int64_t rows, int64_t D,
                                          int64_t F, int E, void* stream);
 
 /* Grouped expert GEMM (the down projection, mixtral_moe_layer.mlir:42):
  * y[r, :] = a[r] . w[e] for the rows of expert e.  a bf16 [rows, K],
- * w bf16 [E, K, N], y bf16 [rows, N]; K % 8 == 0, N % 256 == 0. */
+ * w bf16 [E, K, N], y bf16 [rows, N]; K % 8 == 0, N % 32 == 0. */
 int remora_b200_grouped_gemm_bf16(const void* a, const void* w, void* y, const int32_t* offsets,
                                   int64_t rows, int64_t K, int64_t N, int E, void* stream);
 
@@ -244,7 +246,7 @@ size_t remora_b200_moe_workspace_bytes(int64_t T, int64_t D, int64_t F, int E, i
 /* The whole MoE layer: router -> dispatch -> gather -> SwiGLU grouped GEMM
  * -> down grouped GEMM -> combine, stream-ordered, no host synchronisation.
  * x bf16 [T, D]; wr bf16 [D, E]; wg, wu bf16 [E, D, F]; wd bf16 [E, F, D];
- * out bf16 [T, D].  F % 128 == 0, D % 256 == 0.  The workspace (caller
+ * out bf16 [T, D].  F % 32 == 0, D % 32 == 0.  The workspace (caller
  * owned, 16-byte aligned) holds the routing tables and the dispatched
  * activations. */
 int remora_b200_moe_layer_bf16(const void* x, const void* wr, const void* wg, const void* wu,

@@ -249,15 +249,16 @@ def _i32(*ts):
             raise TypeError("expected a contiguous int32 tensor")
 
 
-def moe_router_topk(x: torch.Tensor, wr: torch.Tensor, k: int):
+def moe_router_topk(x: torch.Tensor, wr: torch.Tensor, k: int, idx: torch.Tensor | None = None,
+                    w: torch.Tensor | None = None):
     """Router logits (increasing-d fp32), top-k indices and softmax weights."""
     _dev(x, wr)
     _bf16(x, wr)
     T, D = x.shape
     E = wr.shape[1]
     x, wr = x.contiguous(), wr.contiguous()
-    idx = torch.empty((T, k), dtype=torch.int32, device=x.device)
-    w = torch.empty((T, k), dtype=torch.float32, device=x.device)
+    idx = torch.empty((T, k), dtype=torch.int32, device=x.device) if idx is None else idx
+    w = torch.empty((T, k), dtype=torch.float32, device=x.device) if w is None else w
     _check(lib().remora_b200_moe_router_topk_bf16(x.data_ptr(), wr.data_ptr(), T, D, E, k,
                                                   idx.data_ptr(), w.data_ptr(), _stream(x)))
     return idx, w
@@ -293,28 +294,29 @@ def moe_gather(x: torch.Tensor, perm: torch.Tensor, k: int) -> torch.Tensor:
 
 
 def grouped_gemm_swiglu(xs: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor,
-                        offsets: torch.Tensor) -> torch.Tensor:
+                        offsets: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """h = silu(xs . wg[e]) * (xs . wu[e]) over each expert's row segment."""
     _dev(xs, wg, wu, offsets)
     _bf16(xs, wg, wu)
     _i32(offsets)
     rows, D = xs.shape
     E, _, F = wg.shape
-    h = torch.empty((rows, F), dtype=torch.bfloat16, device=xs.device)
+    h = torch.empty((rows, F), dtype=torch.bfloat16, device=xs.device) if out is None else out
     _check(lib().remora_b200_grouped_gemm_swiglu_bf16(
         xs.contiguous().data_ptr(), wg.contiguous().data_ptr(), wu.contiguous().data_ptr(),
         h.data_ptr(), offsets.data_ptr(), rows, D, F, E, _stream(xs)))
     return h
 
 
-def grouped_gemm(a: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor) -> torch.Tensor:
+def grouped_gemm(a: torch.Tensor, w: torch.Tensor, offsets: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
     """y = a . w[e] over each expert's row segment (w [E, K, N])."""
     _dev(a, w, offsets)
     _bf16(a, w)
     _i32(offsets)
     rows, K = a.shape
     E, _, N = w.shape
-    y = torch.empty((rows, N), dtype=torch.bfloat16, device=a.device)
+    y = torch.empty((rows, N), dtype=torch.bfloat16, device=a.device) if out is None else out
     _check(lib().remora_b200_grouped_gemm_bf16(a.contiguous().data_ptr(), w.contiguous().data_ptr(),
                                                y.data_ptr(), offsets.data_ptr(), rows, K, N, E,
                                                _stream(a)))

@@ -11,6 +11,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libremora_b200.so")
+CLI = os.path.join(HERE, "remora-b200")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 NVCC_FLAGS = [
@@ -32,7 +33,7 @@ def sources() -> list[str]:
 
 
 def needs_build() -> bool:
-    if not os.path.exists(LIB):
+    if not os.path.exists(LIB) or not os.path.exists(CLI):
         return True
     t = os.path.getmtime(LIB)
     return any(os.path.getmtime(s) > t for s in sources())
@@ -51,7 +52,24 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if r.returncode != 0:
         raise RuntimeError("nvcc failed building libremora_b200.so")
     os.replace(LIB + ".tmp", LIB)
+    build_cli(verbose=verbose)
     return LIB
+
+
+def build_cli(verbose: bool = False) -> str:
+    """The standalone `remora-b200` driver (remora's argv grammar), linked
+    against the in-tree library."""
+    cmd = ["g++", "-O2", "-std=c++17", "-Wall", os.path.join(CSRC, "cli.cpp"), "-o", CLI,
+           "-L" + HERE, "-lremora_b200", "-Wl,-rpath,$ORIGIN"]
+    env = dict(os.environ)
+    env.pop("CC", None)
+    env.pop("CXX", None)
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    if verbose or r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+    if r.returncode != 0:
+        raise RuntimeError("g++ failed building remora-b200")
+    return CLI
 
 
 if __name__ == "__main__":

@@ -235,25 +235,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool raise = mt > m + 8.0f;
       const float alpha = raise ? ((m == -INFINITY) ? 0.0f : ex2(m - mt)) : 1.0f;
       const bool rescale_o = raise && j > 0 && m != -INFINITY;
-      if (__any_sync(0xffffffffu, rescale_o)) {
-        // O holds the products of earlier tiles: PV of tile j-1 was issued
-        // before S of tile j, so it has completed once s_full fired.
-#pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
-          uint32_t o[32];
-          tmem_ld32(t_o + c, o);
-          tmem_ld_wait();
-          const float f = rescale_o ? alpha : 1.0f;
-          uint32_t lo[16], hi[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            lo[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            hi[i] = __float_as_uint(__uint_as_float(o[16 + i]) * f);
-          }
-          tmem_st16(t_o + c, lo);
-          tmem_st16(t_o + c + 16, hi);
-        }
-      }
       if (raise) {
         l *= alpha;
         m = mt;
@@ -272,6 +253,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c)
         tmem_st16(t_s + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&r[c * 16]));
+      if (__any_sync(0xffffffffu, rescale_o)) {
+        // O holds the products of earlier tiles: PV of tile j-1 was issued
+        // before S of tile j, so it has completed once s_full fired; PV of
+        // tile j waits for p_full below.  Done after P is written, when the
+        // S registers are free.
+        const float f = rescale_o ? alpha : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(t_o + c, o);
+          tmem_ld_wait();
+          uint32_t lo[16], hi[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            lo[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            hi[i] = __float_as_uint(__uint_as_float(o[16 + i]) * f);
+          }
+          tmem_st16(t_o + c, lo);
+          tmem_st16(t_o + c + 16, hi);
+        }
+      }
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();

@@ -311,6 +311,123 @@ static int run_attention(const remora_b200_opts* o, remora_b200_report* r, cudaS
   return REMORA_B200_OK;
 }
 
+// --test=moe: the MoE layer of mlir/stablehlo/mixtral_moe_layer.mlir:8-68
+// with bf16 operands.  config "4" (default: T=8192 D=4096 F=14336 E=8 top-2),
+// "5" (T=65536 D=2048 F=1536 E=64 top-8), "mixtral" (the program's own
+// T=512 D=4096 F=14336 E=8 top-2) or "simple" (simple_moe.mlir:16:
+// T=8 D=32 F=64 E=2 top-1).  Tokens N(0,1), weights N(0,0.02), seeded.
+// Validation on up to 16 sampled tokens: router indices exactly as the
+// increasing-d fp32 loop nest gives them, layer output normwise <= 2e-2.
+static int run_moe(const remora_b200_opts* o, remora_b200_report* r, cudaStream_t st) {
+  int64_t T = 8192, D = 4096, F = 14336;
+  int E = 8, k = 2;
+  std::string c = o && o->config ? o->config : "4";
+  if (c == "5") { T = 65536; D = 2048; F = 1536; E = 64; k = 8; }
+  else if (c == "mixtral") { T = 512; }
+  else if (c == "simple") { T = 8; D = 32; F = 64; E = 2; k = 1; }
+  else if (c != "4") return fail(REMORA_B200_ERR_INVALID, "moe: unknown config '%s'", c.c_str());
+  const uint64_t seed = o && o->seed ? o->seed : 42;
+  DevBuf x, wr, wg, wu, wd, out, ws, idx, w;
+  const size_t wsb = remora_b200_moe_workspace_bytes(T, D, F, E, k);
+  int rc;
+  if ((rc = x.alloc(T * D * 2)) || (rc = wr.alloc(D * E * 2)) || (rc = wg.alloc(E * D * F * 2)) ||
+      (rc = wu.alloc(E * D * F * 2)) || (rc = wd.alloc(E * F * D * 2)) ||
+      (rc = out.alloc(T * D * 2)) || (rc = ws.alloc(wsb)) || (rc = idx.alloc(T * k * 4)) ||
+      (rc = w.alloc(T * k * 4)))
+    return rc;
+  if ((rc = remora_b200_fill_normal(x.p, T * D, 1, stream_key(seed, 30), 0, 1, st)) ||
+      (rc = remora_b200_fill_normal(wr.p, D * E, 1, stream_key(seed, 31), 0, 0.02, st)) ||
+      (rc = remora_b200_fill_normal(wg.p, E * D * F, 1, stream_key(seed, 32), 0, 0.02, st)) ||
+      (rc = remora_b200_fill_normal(wu.p, E * D * F, 1, stream_key(seed, 33), 0, 0.02, st)) ||
+      (rc = remora_b200_fill_normal(wd.p, E * F * D, 1, stream_key(seed, 34), 0, 0.02, st)))
+    return rc;
+  double ms = 0;
+  rc = time_iters(o, st, [&] {
+    return remora_b200_moe_layer_bf16(x.p, wr.p, wg.p, wu.p, wd.p, out.p, T, D, F, E, k, ws.p,
+                                      wsb, st);
+  }, &ms);
+  if (rc) return rc;
+  ErrStat e;
+  bool idx_ok = true;
+  if (o && o->validate) {
+    if ((rc = remora_b200_moe_router_topk_bf16(x.p, wr.p, T, D, E, k, (int32_t*)idx.p,
+                                               (float*)w.p, st)))
+      return rc;
+    RB_CUDA(cudaStreamSynchronize(st));
+    std::vector<uint16_t> hx(T * D), hwr(D * E), ho(T * D);
+    std::vector<int32_t> hidx(T * k);
+    RB_CUDA(cudaMemcpy(hx.data(), x.p, hx.size() * 2, cudaMemcpyDeviceToHost));
+    RB_CUDA(cudaMemcpy(hwr.data(), wr.p, hwr.size() * 2, cudaMemcpyDeviceToHost));
+    RB_CUDA(cudaMemcpy(ho.data(), out.p, ho.size() * 2, cudaMemcpyDeviceToHost));
+    RB_CUDA(cudaMemcpy(hidx.data(), idx.p, hidx.size() * 4, cudaMemcpyDeviceToHost));
+    const int ns = (int)std::min<int64_t>(T, 16);
+    std::vector<std::vector<uint16_t>> eg(E), eu(E), ed(E);
+    std::vector<double> ref(D), hrow(F), g(F), u(F);
+    double worst = 0, scale = 0;
+    for (int si = 0; si < ns; ++si) {
+      const int64_t t = (int64_t)(host_mix64(stream_key(seed, 97) + si) % (uint64_t)T);
+      const uint16_t* xr = hx.data() + t * D;
+      std::vector<float> lg(E, 0.0f);
+      for (int64_t d = 0; d < D; ++d)
+        for (int ee = 0; ee < E; ++ee) lg[ee] = lg[ee] + bf16_to_f32(xr[d]) * bf16_to_f32(hwr[d * E + ee]);
+      std::vector<int> sel;
+      std::vector<float> sv;
+      std::vector<char> used(E, 0);
+      for (int j = 0; j < k; ++j) {
+        int best = -1;
+        for (int ee = 0; ee < E; ++ee)
+          if (!used[ee] && (best < 0 || lg[ee] > lg[best])) best = ee;  // ties -> lower index
+        used[best] = 1;
+        sel.push_back(best);
+        sv.push_back(lg[best]);
+        if (hidx[t * k + j] != best) idx_ok = false;
+      }
+      float m = -INFINITY, ssum = 0.0f;
+      for (float v : sv) m = v > m ? v : m;
+      std::vector<float> ex(k);
+      for (int j = 0; j < k; ++j) { ex[j] = expf(sv[j] - m); ssum = ssum + ex[j]; }
+      std::fill(ref.begin(), ref.end(), 0.0);
+      for (int j = 0; j < k; ++j) {
+        const int ee = sel[j];
+        if (eg[ee].empty()) {
+          eg[ee].resize(D * F); eu[ee].resize(D * F); ed[ee].resize(F * D);
+          RB_CUDA(cudaMemcpy(eg[ee].data(), (uint16_t*)wg.p + ee * D * F, D * F * 2, cudaMemcpyDeviceToHost));
+          RB_CUDA(cudaMemcpy(eu[ee].data(), (uint16_t*)wu.p + ee * D * F, D * F * 2, cudaMemcpyDeviceToHost));
+          RB_CUDA(cudaMemcpy(ed[ee].data(), (uint16_t*)wd.p + ee * F * D, F * D * 2, cudaMemcpyDeviceToHost));
+        }
+        std::fill(g.begin(), g.end(), 0.0);
+        std::fill(u.begin(), u.end(), 0.0);
+        for (int64_t d = 0; d < D; ++d) {
+          const double a = bf16_to_f32(xr[d]);
+          const uint16_t* gr = eg[ee].data() + d * F;
+          const uint16_t* ur = eu[ee].data() + d * F;
+          for (int64_t f = 0; f < F; ++f) { g[f] += a * bf16_to_f32(gr[f]); u[f] += a * bf16_to_f32(ur[f]); }
+        }
+        for (int64_t f = 0; f < F; ++f) hrow[f] = g[f] / (1.0 + std::exp(-g[f])) * u[f];
+        const double wj = ex[j] / ssum;
+        for (int64_t f = 0; f < F; ++f) {
+          const uint16_t* dr = ed[ee].data() + f * D;
+          const double hv = wj * hrow[f];
+          for (int64_t d = 0; d < D; ++d) ref[d] += hv * bf16_to_f32(dr[d]);
+        }
+      }
+      for (int64_t d = 0; d < D; ++d) {
+        worst = std::max(worst, std::fabs(bf16_to_f32(ho[t * D + d]) - ref[d]));
+        scale = std::max(scale, std::fabs(ref[d]));
+      }
+      e.n += D;
+    }
+    e.max_abs = worst;
+    e.max_rel = scale > 0 ? worst / scale : worst;
+  }
+  finish(r, ms, 6.0 * D * F * T * k, e, 2e-2, o ? o->validate : 0, "moe layer bf16", "TFLOP/s");
+  if (o && o->validate && !idx_ok) {
+    r->passed = 0;
+    snprintf(r->detail, sizeof(r->detail), "moe layer: router indices differ from the loop nest");
+  }
+  return REMORA_B200_OK;
+}
+
 }  // namespace rb
 
 extern "C" const char* remora_b200_last_error(void) { return rb::t_last_error; }
@@ -333,7 +450,7 @@ extern "C" int remora_b200_recognise(const char* test) {
   if (!test) return 0;
   std::string t = test;
   return t == "elementwise" || t == "projection" || t == "elementwise_chain" || t == "gemm" ||
-         t == "attention";
+         t == "attention" || t == "moe";
 }
 
 extern "C" int remora_b200_run_test(const char* test, const remora_b200_opts* o,
@@ -357,6 +474,8 @@ extern "C" int remora_b200_run_test(const char* test, const remora_b200_opts* o,
     rc = run_gemm(o, r, st);
   else if (t == "attention")
     rc = run_attention(o, r, st);
+  else if (t == "moe")
+    rc = run_moe(o, r, st);
   else
     rc = fail(REMORA_B200_ERR_UNSUPPORTED, "--run-gpu for test '%s' not recognised", test);
   cudaStreamDestroy(st);

@@ -22,7 +22,6 @@ namespace moe {
 // fp32, so fmaf(a, b, acc) == acc + a*b here.
 constexpr int kRouterThreads = 256;
 constexpr int kRouterDC = 64;           // d per shared-memory chunk
-constexpr int kRowPad = kRouterDC + 8;  // bf16 elements per padded token row
 
 __device__ __forceinline__ bool topk_before(float a, int ia, float b, int ib) {
   const bool an = a != a, bn = b != b;
@@ -31,92 +30,121 @@ __device__ __forceinline__ bool topk_before(float a, int ia, float b, int ib) {
   return ia < ib;
 }
 
-// G token groups x E experts threads; each thread owns R tokens (R
-// independent chains).  Shared memory per d-chunk: the block's tokens
-// [TPB][kRowPad] and the router chunk in its natural [kRouterDC][E] layout
-// (a warp then reads consecutive experts: no bank conflicts, no transpose).
-template <int R>
-__global__ void __launch_bounds__(kRouterThreads)
-    k_router_topk(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr, int T, int D,
-                  int E, int k, int G, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
-  extern __shared__ __align__(16) uint8_t sm_raw[];
-  const int TPB = G * R;
-  uint16_t* xs = reinterpret_cast<uint16_t*>(sm_raw);                 // [TPB][kRowPad]
-  uint16_t* ws = xs + TPB * kRowPad;                                  // [kRouterDC][E]
-  float* lg = reinterpret_cast<float*>(ws + ((kRouterDC * E + 7) & ~7));  // [TPB][E]
-  const int tid = threadIdx.x;
-  const int e = tid % E, g = tid / E;
-  const bool active = g < G;
-  const int t0 = blockIdx.x * TPB;
-  float acc[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) acc[r] = 0.0f;
+// Register-blocked router.  Thread (token group tg, expert group eg) owns an
+// RT x 8 block of (token, expert) accumulators: tokens tg*RT .. +RT-1 of the
+// block, experts eg*8 .. eg*8+7.  Each accumulator is still one serial fp32
+// chain over d in increasing order (bit-exact), but a 4-d step costs RT + 8
+// shared loads for 32*RT FMAs.  Tokens and router chunks are converted to f32
+// once while staging.  NG = expert groups per token, a power of two <= 32:
+// the NG lanes of a token are adjacent, so top-k is a segmented shuffle.
+constexpr int kRouterDCh = 32;             // d per chunk
+constexpr int kRowPadF = kRouterDCh + 4;   // padded f32 row (conflict-free 16-byte loads)
 
-  for (int d0 = 0; d0 < D; d0 += kRouterDC) {
-    const int dc = min(kRouterDC, D - d0);
-    // tokens chunk: TPB rows x dc bf16, 16-byte pieces (D % 8 == 0)
-    for (int i = tid; i < TPB * (kRouterDC / 8); i += blockDim.x) {
-      const int row = i / (kRouterDC / 8), c8 = (i % (kRouterDC / 8)) * 8;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (t0 + row < T && c8 < dc)
-        v = *reinterpret_cast<const uint4*>(x + (int64_t)(t0 + row) * D + d0 + c8);
-      *reinterpret_cast<uint4*>(xs + row * kRowPad + c8) = v;
+template <int RT, int NG>
+__global__ void __launch_bounds__(kRouterThreads, 1)
+    k_router_topk(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr, int T, int D,
+                  int E, int k, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  constexpr int TG = kRouterThreads / NG;  // token groups per block
+  constexpr int TPB = TG * RT;             // tokens per block
+  constexpr int EP = NG * 8;               // padded expert count
+  float* xs = reinterpret_cast<float*>(sm_raw);  // [TPB][kRowPadF]
+  float* ws = xs + TPB * kRowPadF;               // [EP][kRowPadF] (transposed chunk)
+  const int tid = threadIdx.x;
+  const int eg = tid % NG, tg = tid / NG;
+  const int t0 = blockIdx.x * TPB;
+  float acc[RT][8];
+#pragma unroll
+  for (int r = 0; r < RT; ++r)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[r][i] = 0.0f;
+
+  // The next chunk's global loads are issued into registers before the
+  // current chunk is computed, so their latency overlaps the FMAs.
+  constexpr int XPT = (TPB * (kRouterDCh / 8) + kRouterThreads - 1) / kRouterThreads;
+  constexpr int WPT = (kRouterDCh * EP + kRouterThreads - 1) / kRouterThreads;
+  uint4 xpre[XPT];
+  uint16_t wpre[WPT];
+  auto load_chunk = [&](int d0) {
+    const int dc = min(kRouterDCh, D - d0);
+#pragma unroll
+    for (int j = 0; j < XPT; ++j) {
+      const int i = tid + j * kRouterThreads;
+      const int row = i / (kRouterDCh / 8), c8 = (i % (kRouterDCh / 8)) * 8;
+      xpre[j] = make_uint4(0, 0, 0, 0);
+      if (i < TPB * (kRouterDCh / 8) && t0 + row < T && c8 < dc)
+        xpre[j] = *reinterpret_cast<const uint4*>(x + (int64_t)(t0 + row) * D + d0 + c8);
     }
-    // router chunk rows d0 .. d0+dc-1 (contiguous in global memory)
-    if ((E & 7) == 0) {
-      const int n8 = kRouterDC * E / 8;
-      for (int i = tid; i < n8; i += blockDim.x) {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (i * 8 < dc * E) v = *reinterpret_cast<const uint4*>(wr + (int64_t)d0 * E + i * 8);
-        *reinterpret_cast<uint4*>(ws + i * 8) = v;
-      }
-    } else {
-      for (int i = tid; i < kRouterDC * E; i += blockDim.x)
-        ws[i] = i < dc * E ? wr[(int64_t)d0 * E + i] : (uint16_t)0;
+#pragma unroll
+    for (int j = 0; j < WPT; ++j) {
+      const int i = tid + j * kRouterThreads;
+      const int dd = i / EP, ee = i % EP;
+      wpre[j] = (i < kRouterDCh * EP && dd < dc && ee < E) ? wr[(int64_t)(d0 + dd) * E + ee]
+                                                             : (uint16_t)0;
     }
+  };
+  auto store_chunk = [&]() {
+#pragma unroll
+    for (int j = 0; j < XPT; ++j) {
+      const int i = tid + j * kRouterThreads;
+      if (i >= TPB * (kRouterDCh / 8)) break;
+      const int row = i / (kRouterDCh / 8), c8 = (i % (kRouterDCh / 8)) * 8;
+      // token q = tg*RT + r lives in smem row r*TG + tg: the token groups of a
+      // warp then read adjacent rows (conflict-free 16-byte loads)
+      const int srow = (row % RT) * TG + row / RT;
+      const uint4 v = xpre[j];
+      float4* dst = reinterpret_cast<float4*>(xs + srow * kRowPadF + c8);
+      dst[0] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u),
+                           __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
+      dst[1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xffff0000u),
+                           __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xffff0000u));
+    }
+#pragma unroll
+    for (int j = 0; j < WPT; ++j) {
+      const int i = tid + j * kRouterThreads;
+      if (i >= kRouterDCh * EP) break;
+      const int dd = i / EP, ee = i % EP;
+      // expert ee = eg*8 + q lives in row q*NG + eg (adjacent rows across eg)
+      ws[((ee & 7) * NG + (ee >> 3)) * kRowPadF + dd] = __uint_as_float((uint32_t)wpre[j] << 16);
+    }
+  };
+
+  load_chunk(0);
+  for (int d0 = 0; d0 < D; d0 += kRouterDCh) {
+    store_chunk();
     __syncthreads();
-    if (active) {
+    if (d0 + kRouterDCh < D) load_chunk(d0 + kRouterDCh);
 #pragma unroll 2
-      for (int dd = 0; dd < kRouterDC; dd += 8) {
-        float wv[8];
+    for (int dd = 0; dd < kRouterDCh; dd += 4) {
+      float4 wv[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) wv[q] = __uint_as_float((uint32_t)ws[(dd + q) * E + e] << 16);
+      for (int i = 0; i < 8; ++i)
+        wv[i] = *reinterpret_cast<const float4*>(ws + (i * NG + eg) * kRowPadF + dd);
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const uint4 xv = *reinterpret_cast<const uint4*>(xs + (g * R + r) * kRowPad + dd);
-          const uint32_t xq[4] = {xv.x, xv.y, xv.z, xv.w};
+      for (int r = 0; r < RT; ++r) {
+        const float4 xv = *reinterpret_cast<const float4*>(xs + (r * TG + tg) * kRowPadF + dd);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            acc[r] = fmaf(__uint_as_float(xq[q] << 16), wv[2 * q], acc[r]);
-            acc[r] = fmaf(__uint_as_float(xq[q] & 0xffff0000u), wv[2 * q + 1], acc[r]);
-          }
+        for (int i = 0; i < 8; ++i) {
+          acc[r][i] = fmaf(xv.x, wv[i].x, acc[r][i]);
+          acc[r][i] = fmaf(xv.y, wv[i].y, acc[r][i]);
+          acc[r][i] = fmaf(xv.z, wv[i].z, acc[r][i]);
+          acc[r][i] = fmaf(xv.w, wv[i].w, acc[r][i]);
         }
       }
     }
     __syncthreads();
   }
-  if (active) {
-#pragma unroll
-    for (int r = 0; r < R; ++r) lg[(g * R + r) * E + e] = acc[r];
-  }
-  __syncthreads();
 
-  // warp-shuffle top-k over each token's E logits, then softmax over the k
-  const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
-  const int per_lane = (E + 31) / 32;  // <= 8
-  for (int tok = warp; tok < TPB; tok += nwarps) {
-    const int t = t0 + tok;
-    if (t >= T) break;
-    float v[8];
-    int vi[8];
+  // top-k per token over the NG lanes of its group (8 candidates per lane)
+  const int lane = tid & 31;
+  const unsigned gmask = (NG == 32) ? 0xffffffffu : (((1u << NG) - 1u) << (lane & ~(NG - 1)));
+#pragma unroll
+  for (int r = 0; r < RT; ++r) {  // unrolled: acc[r][i] stays in registers
+    const int t = t0 + tg * RT + r;
     uint32_t used = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int ei = lane + 32 * i;
-      vi[i] = ei;
-      v[i] = (i < per_lane && ei < E) ? lg[tok * E + ei] : 0.0f;
-      if (!(i < per_lane && ei < E)) used |= 1u << i;
-    }
+    for (int i = 0; i < 8; ++i)
+      if (eg * 8 + i >= E) used |= 1u << i;
     float sel_v[16];
     int sel_i[16];
     for (int j = 0; j < k; ++j) {
@@ -124,14 +152,15 @@ __global__ void __launch_bounds__(kRouterThreads)
       int bi = 0x7fffffff;
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        if (!(used >> i & 1u) && (bi == 0x7fffffff || topk_before(v[i], vi[i], bv, bi))) {
-          bv = v[i];
-          bi = vi[i];
+        if (!(used >> i & 1u) &&
+            (bi == 0x7fffffff || topk_before(acc[r][i], eg * 8 + i, bv, bi))) {
+          bv = acc[r][i];
+          bi = eg * 8 + i;
         }
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      for (int off = NG / 2; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(gmask, bv, off, NG);
+        const int oi = __shfl_xor_sync(gmask, bi, off, NG);
         if (oi != 0x7fffffff && (bi == 0x7fffffff || topk_before(ov, oi, bv, bi))) {
           bv = ov;
           bi = oi;
@@ -139,9 +168,9 @@ __global__ void __launch_bounds__(kRouterThreads)
       }
       sel_v[j] = bv;
       sel_i[j] = bi;
-      if ((bi & 31) == lane) used |= 1u << (bi >> 5);
+      if (bi >> 3 == eg) used |= 1u << (bi & 7);
     }
-    if (lane == 0) {
+    if (eg == 0 && t < T) {
       // stablehlo.reduce maximum (init -inf), exp, reduce add (init 0), divide
       float m = -INFINITY;
       for (int j = 0; j < k; ++j) m = (sel_v[j] != sel_v[j] || sel_v[j] > m) ? sel_v[j] : m;

@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(GThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm->tmem_empty[acc]);
         }
-        if (valid) {
+        if (valid && ti.n * kColsPerTile + c * 32 < s.N) {  // N % 32 == 0
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
           for (int i = 0; i < 4; ++i)

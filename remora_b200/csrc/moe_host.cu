@@ -19,25 +19,30 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
   RB_CHECK_ARG(x && wr && idx && w, "router: null pointer");
   RB_CHECK_ARG(aligned16(x), "router: x must be 16-byte aligned");
   RB_CHECK_ARG(T < (1ll << 31) && D < (1ll << 31), "router: sizes exceed 2^31");
-  int G = kRouterThreads / E;
-  if (G > 32) G = 32;
-  if (G < 1) G = 1;
-  const int R = E <= 16 ? 4 : (E <= 32 ? 8 : 16);  // tokens per thread: 64-128 per block
-  const int threads = ((G * E + 31) / 32) * 32;
-  const int TPB = G * R;
-  const size_t smem = (size_t)TPB * kRowPad * 2 + (size_t)((kRouterDC * E + 7) & ~7) * 2 +
-                      (size_t)TPB * E * 4;
-  const int64_t grid = (T + TPB - 1) / TPB;
+  // expert groups of 8 per token (power of two) and tokens per thread
+  int ng = 1;
+  while (ng * 8 < E) ng *= 2;
+  const int rt = ng >= 8 ? 4 : (ng >= 2 ? 2 : 1);
+  const int tpb = (kRouterThreads / ng) * rt;
+  const size_t smem = ((size_t)tpb + (size_t)ng * 8) * kRowPadF * 4;
+  const int64_t grid = (T + tpb - 1) / tpb;
   auto launch = [&](auto kern) -> int {
     if (smem > 48 * 1024)
       RB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<(unsigned)grid, threads, smem, st>>>(static_cast<const uint16_t*>(x),
-                                               static_cast<const uint16_t*>(wr), (int)T, (int)D,
-                                               E, k, G, idx, w);
+    kern<<<(unsigned)grid, kRouterThreads, smem, st>>>(static_cast<const uint16_t*>(x),
+                                                       static_cast<const uint16_t*>(wr), (int)T,
+                                                       (int)D, E, k, idx, w);
     return REMORA_B200_OK;
   };
-  int rc = R == 4 ? launch(k_router_topk<4>) : R == 8 ? launch(k_router_topk<8>)
-                                                     : launch(k_router_topk<16>);
+  int rc;
+  switch (ng) {
+    case 1: rc = launch(k_router_topk<1, 1>); break;
+    case 2: rc = launch(k_router_topk<2, 2>); break;
+    case 4: rc = launch(k_router_topk<2, 4>); break;
+    case 8: rc = launch(k_router_topk<4, 8>); break;
+    case 16: rc = launch(k_router_topk<4, 16>); break;
+    default: rc = launch(k_router_topk<4, 32>); break;
+  }
   if (rc) return rc;
   RB_LAUNCH_CHECK();
   return REMORA_B200_OK;
@@ -92,9 +97,9 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   const int S = n_seg < 0 ? E : n_seg;
   RB_CHECK_ARG(E >= 1 && E <= GMaxE, "grouped_gemm: E=%d unsupported (1..%d)", E, GMaxE);
   RB_CHECK_ARG(S >= 1 && S <= GMaxE, "grouped_gemm: %d segments unsupported (1..%d)", S, GMaxE);
-  RB_CHECK_ARG(rows >= 0 && K > 0 && N > 0 && K % 8 == 0 && N % cols == 0,
-               "grouped_gemm: need K %% 8 == 0 and N %% %d == 0 (K=%lld N=%lld)", cols,
-               (long long)K, (long long)N);
+  RB_CHECK_ARG(rows >= 0 && K > 0 && N > 0 && K % 8 == 0 && N % 32 == 0,
+               "grouped_gemm: need K %% 8 == 0 and N %% 32 == 0 (K=%lld N=%lld)", (long long)K,
+               (long long)N);
   RB_CHECK_ARG(rows < (1ll << 31) && K < (1ll << 31) && N < (1ll << 31),
                "grouped_gemm: sizes exceed 2^31");
   if (rows == 0) return REMORA_B200_OK;
@@ -126,7 +131,7 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   sh.E = E;
   sh.S = S;
   sh.seg_expert = seg_expert;
-  sh.tiles_n = (int)(N / cols);
+  sh.tiles_n = (int)((N + cols - 1) / cols);
   sh.num_kb = (int)((K + GBK - 1) / GBK);
   sh.offsets = offsets;
   sh.out = static_cast<uint16_t*>(out);

@@ -213,3 +213,19 @@ def test_grouped_gemm_segments_match_expert_order(rb, orc):
     h = rb.grouped_gemm_swiglu_segments(from_np_bf16(xs[order]), Wg, Wu, so, se)
     y = to_np_bf16(rb.grouped_gemm_segments(h, Wd, so, se))
     assert np.array_equal(y, y_ref[order])
+
+
+def test_moe_layer_simple_moe_shape(rb, orc):
+    """simple_moe.mlir:16 shapes (T=8, D=32, F=64, E=2, top-1): tiles wider
+    than the matrices, column guards in the epilogues."""
+    x, wr, wg, wu, wd = _moe_inputs(orc, 8, 32, 64, 2)
+    out = rb.moe_layer(*(from_np_bf16(a) for a in (x, wr, wg, wu, wd)), k=1)
+    rb.synchronize_and_check()
+    *_, ref = orc.moe_layer_bf16(x, wr, wg, wu, wd, 1)
+    assert norm_err(orc.bf16_to_f32(to_np_bf16(out)), orc.bf16_to_f32(ref)) <= TOL
+
+
+@pytest.mark.parametrize("cfg", ["simple", "mixtral", "4"])
+def test_run_test_moe_configs(rb, cfg):
+    rep = rb.run_test("moe", config=cfg, iters=2, warmup=1)
+    assert rep["passed"] and rep["max_rel_err"] <= TOL and rep["checked"] > 0
