@@ -487,9 +487,17 @@ def bench_moe_ep(args, world, rank, local):
     lws = (torch.empty(rb.moe_workspace_bytes(T, D, F, E, k), dtype=torch.uint8, device=dev)
            if world == 1 else None)
 
+    pep = None
+    if world > 1 and args.ep_mode == "p2p":
+        from remora_b200.ep_p2p import PeerEP
+
+        pep = PeerEP(tl, D, F, E, k, device=dev)
+
     def step():
         if world == 1:
             rb.moe_layer(x, wr, wg, wu, wd, k, out=out, workspace=lws)
+        elif pep is not None:
+            out.copy_(pep.forward(x, wr, wg, wu, wd))
         else:
             out.copy_(moe_ep_forward(x, wr, wg, wu, wd, k, E, chunks=args.ep_chunks or None))
 
@@ -530,7 +538,8 @@ def bench_moe_ep(args, world, rank, local):
         "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, bf16)",
         "config": {"workload": f"expert-parallel MoE config 5: T={T} D={D} F={F} E={E} top-{k}, "
                                f"{Epr} experts and {tl} tokens per GPU",
-                   "parallelism": f"EP{world} (NCCL all-to-all)" if world > 1 else "single GPU",
+                   "parallelism": (f"EP{world} ({'NVLink peer-memory scatter/combine' if pep else 'NCCL all-to-all'})"
+                                   if world > 1 else "single GPU"),
                    "ep_chunks": args.ep_chunks or "default",
                    "expert_flop_per_step": flop},
         "roofline": {"bound": "tensor", "achieved": per_gpu_tf, "peak": peaks["bf16_tflops"],
@@ -707,6 +716,8 @@ def main():
     ap.add_argument("--workload", choices=["gemm", "elementwise", "moe", "moe_ep", "attention"],
                     default="gemm")
     ap.add_argument("--moe-config", choices=sorted(MOE_CONFIGS), default="4")
+    ap.add_argument("--ep-mode", choices=["p2p", "nccl"], default="p2p",
+                    help="moe_ep: token exchange by the library's peer-memory kernels or NCCL")
     ap.add_argument("--ep-chunks", type=int, default=0,
                     help="moe_ep: token pieces per layer for comm/compute overlap (0 = default)")
     ap.add_argument("--size", type=int, default=0,

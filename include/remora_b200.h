@@ -254,6 +254,48 @@ int remora_b200_moe_layer_bf16(const void* x, const void* wr, const void* wg, co
                                int k, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Expert-parallel MoE over NVLink peer memory (P <= 8 ranks, one per GPU).
+ * The reference has no multi-GPU path (one device, gpu_tests.cpp:102-104);
+ * these replace an NCCL all-to-all for the token exchange.  Every rank holds
+ * buffers its peers can address (e.g. torch symmetric memory): recv
+ * [P][cap][D] bf16, meta [P][E/P+1] int32, y [T_local*k][D] bf16 and flags
+ * [P] int32 (zero-initialised once).  *_ptrs are host arrays of the P
+ * ranks' device addresses of that buffer.  Only plain loads and stores
+ * reach peer memory.
+ * --------------------------------------------------------------------- */
+
+/* Copies this rank's n dispatched rows (x[perm[p]/k], dispatch order of
+ * remora_b200_moe_dispatch over all E experts) into region `rank` of the
+ * owning rank's recv buffer, and writes that rank's meta[rank] (rows per
+ * local expert, then the first dispatch position of those rows).
+ * n <= cap; cap = the most rows one rank can send (T_local * k). */
+int remora_b200_moe_ep_scatter_bf16(const void* x, const int32_t* perm, const int32_t* offsets,
+                                    int64_t n, int k, int64_t D, int E, int P, int rank,
+                                    int64_t cap, const uint64_t* recv_ptrs,
+                                    const uint64_t* meta_ptrs, void* stream);
+
+/* Stream-ordered barrier: publishes `epoch` (increasing per call) in every
+ * peer's flags[rank], then waits until all of this rank's flags reach it.
+ * Bounded: a wait longer than 2 s records a timeout that
+ * remora_b200_device_status() reports (REMORA_B200_ERR_TIMEOUT). */
+int remora_b200_moe_ep_barrier(int32_t* flags, const uint64_t* flag_ptrs, int P, int rank,
+                               int epoch, void* stream);
+
+/* Builds the 5*(P*Epr) int32 segment table of the received rows from this
+ * rank's meta: start, end, local expert, destination row, source rank. */
+int remora_b200_moe_ep_segments(const int32_t* meta, int P, int Epr, int64_t cap, int32_t* seg,
+                                void* stream);
+
+/* The local experts over the received rows: SwiGLU grouped GEMM into h
+ * ([P*cap, F], recv's row layout), then the down grouped GEMM, each output
+ * row stored into its source rank's y at the row it was dispatched from.
+ * wg, wu [Epr, D, F]; wd [Epr, F, D] (this rank's experts). */
+int remora_b200_moe_ep_experts_bf16(const void* recv, const void* wg, const void* wu,
+                                    const void* wd, void* h, const int32_t* seg, int P, int Epr,
+                                    int64_t cap, int64_t D, int64_t F, const uint64_t* y_ptrs,
+                                    void* stream);
+
+/* ------------------------------------------------------------------------
  * Seeded input generator (device side of the counter-based generator the
  * tests and benchmarks use; one stream key per tensor)
  * --------------------------------------------------------------------- */

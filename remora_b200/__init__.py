@@ -82,6 +82,10 @@ _SIGNATURES = {
     "remora_b200_moe_workspace_bytes": ([I64, I64, I64, I, I], ctypes.c_size_t),
     "remora_b200_moe_layer_bf16": ([P, P, P, P, P, P, I64, I64, I64, I, I, P, ctypes.c_size_t, P],
                                    I),
+    "remora_b200_moe_ep_scatter_bf16": ([P, P, P, I64, I, I64, I, I, I, I64, P, P, P], I),
+    "remora_b200_moe_ep_barrier": ([P, P, I, I, I, P], I),
+    "remora_b200_moe_ep_segments": ([P, I, I, I64, P, P], I),
+    "remora_b200_moe_ep_experts_bf16": ([P, P, P, P, P, P, I, I, I64, I64, I64, P, P], I),
     "remora_b200_device_status": ([], I),
     "remora_b200_fill_normal": ([P, I64, I, U64, D, D, P], I),
     "remora_b200_fill_uniform": ([P, I64, I, U64, D, D, P], I),

@@ -9,4 +9,5 @@
 #include "moe_gemm.cu"
 #include "moe_host.cu"
 #include "moe_noalloc.cu"
+#include "moe_ep.cu"
 #include "dispatch.cu"

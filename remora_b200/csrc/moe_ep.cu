@@ -1,0 +1,195 @@
+// moe_ep.cu -- expert-parallel dispatch and combine over NVLink peer memory.
+//
+// Each rank owns, in memory every peer can address (symmetric buffers):
+//   recv  [P][cap][D] bf16  region s receives the rows rank s routes here
+//   meta  [P][Epr+1]  int32 region s: rows per local expert, then the row
+//                            of rank s's dispatch order they start at
+//   y     [T_local*k][D]    the expert outputs of this rank's own rows,
+//                            written back by the ranks that computed them
+//   flags [P]         int32 barrier epochs, slot s written by rank s
+// A layer: scatter (this rank's dispatched rows -> peers' recv, no local
+// gather copy, no host round trip) -> barrier -> grouped GEMMs over
+// (source, local expert) segments, the down GEMM storing each output row
+// straight into its source rank's y -> barrier -> local combine.
+// Plain loads and stores to peer addresses only (no TMA, no multicast).
+// The barrier's waits are bounded: after the limit the kernel records
+// error 1 in the device error word and returns.
+#include "runtime.cuh"
+
+namespace rb {
+namespace moe {
+
+// Rows of this rank in dispatch order p = 0 .. n-1 (expert-sorted); the
+// destination rank is e / Epr, the row index inside region `rank` of that
+// peer is p - offsets[q * Epr].  Token row = perm[p] / k.
+__global__ void k_ep_scatter(const uint16_t* __restrict__ x, const int32_t* __restrict__ perm,
+                             const int32_t* __restrict__ offsets, int64_t n, int k, int D,
+                             int Epr, int P, int rank, int64_t cap, PeerPtrs recv,
+                             PeerPtrs meta) {
+  // metadata first (block 0): counts per local expert and the base row
+  if (blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < P * (Epr + 1); i += blockDim.x) {
+      const int q = i / (Epr + 1), j = i % (Epr + 1);
+      const int v = j < Epr ? offsets[q * Epr + j + 1] - offsets[q * Epr + j] : offsets[q * Epr];
+      reinterpret_cast<int32_t*>(meta.p[q])[rank * (Epr + 1) + j] = v;
+    }
+  }
+  const int lane = threadIdx.x & 31;
+  const int64_t wpb = blockDim.x >> 5;
+  for (int64_t p = blockIdx.x * wpb + (threadIdx.x >> 5); p < n; p += (int64_t)gridDim.x * wpb) {
+    // destination rank: the last q with offsets[q * Epr] <= p
+    int q = 0;
+    while (q + 1 < P && offsets[(q + 1) * Epr] <= p) ++q;
+    const int64_t i = p - offsets[q * Epr];
+    const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(perm[p] / k) * D);
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(recv.p[q]) +
+                                          ((int64_t)rank * cap + i) * D);
+    for (int c = lane; c < D / 8; c += 32) dst[c] = __ldg(src + c);
+  }
+}
+
+// Barrier over P ranks: publish `epoch` in every peer's flag slot `rank`,
+// then wait (bounded) until every slot of this rank's flags holds >= epoch.
+__global__ void k_ep_barrier(int32_t* flags, PeerPtrs peer_flags, int P, int rank, int epoch) {
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  __threadfence_system();  // this rank's earlier stores (previous kernels) first
+  if (lane < P) {
+    int32_t* f = reinterpret_cast<int32_t*>(peer_flags.p[lane]) + rank;
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(f), "r"(epoch) : "memory");
+  }
+  if (lane < P) {
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 0;; ++it) {
+      int32_t v;
+      asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + lane) : "memory");
+      if (v - epoch >= 0) break;
+      if ((it & 63u) == 63u && globaltimer() - t0 > kWaitLimitNs) {
+        atomicExch(&g_device_error, 1);
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  __syncwarp();
+  __threadfence_system();
+}
+
+// Segments of the received rows, (source s, local expert e) in that order:
+// start = s*cap + rows of s for experts < e, end = start + count, expert e,
+// output row in s's y = base_s + rows of s for experts < e.
+__global__ void k_ep_segments(const int32_t* __restrict__ meta, int P, int Epr, int64_t cap,
+                              int32_t* seg_start, int32_t* seg_end, int32_t* seg_expert,
+                              int32_t* seg_dst_row, int32_t* seg_dst_rank) {
+  for (int s = threadIdx.x; s < P; s += blockDim.x) {
+    const int32_t* m = meta + s * (Epr + 1);
+    int32_t run = 0;
+    for (int e = 0; e < Epr; ++e) {
+      const int q = s * Epr + e;
+      seg_start[q] = (int32_t)(s * cap) + run;
+      seg_end[q] = seg_start[q] + m[e];
+      seg_expert[q] = e;
+      seg_dst_row[q] = m[Epr] + run;
+      seg_dst_rank[q] = s;
+      run += m[e];
+    }
+  }
+}
+
+}  // namespace moe
+}  // namespace rb
+
+using namespace rb;
+using namespace rb::moe;
+
+namespace {
+
+int peer_ptrs(const uint64_t* host, int P, PeerPtrs* out, const char* what) {
+  RB_CHECK_ARG(host, "moe_ep: null %s address list", what);
+  *out = PeerPtrs{};
+  for (int i = 0; i < P; ++i) {
+    RB_CHECK_ARG(host[i] != 0 && (host[i] & 15u) == 0, "moe_ep: %s address of rank %d is null "
+                 "or not 16-byte aligned", what, i);
+    out->p[i] = host[i];
+  }
+  return REMORA_B200_OK;
+}
+
+}  // namespace
+
+extern "C" int remora_b200_moe_ep_scatter_bf16(const void* x, const int32_t* perm,
+                                               const int32_t* offsets, int64_t n, int k,
+                                               int64_t D, int E, int P, int rank, int64_t cap,
+                                               const uint64_t* recv_ptrs,
+                                               const uint64_t* meta_ptrs, void* stream) {
+  clear_error();
+  RB_CHECK_ARG(P >= 1 && P <= 8 && rank >= 0 && rank < P && E % P == 0 && E <= GMaxE,
+               "moe_ep_scatter: bad P=%d rank=%d E=%d", P, rank, E);
+  RB_CHECK_ARG(n >= 0 && k >= 1 && D > 0 && D % 8 == 0 && cap >= 0 && n <= cap,
+               "moe_ep_scatter: bad sizes");
+  RB_CHECK_ARG((int64_t)P * cap < (1ll << 31), "moe_ep_scatter: P*cap exceeds 2^31 rows");
+  PeerPtrs rp, mp;
+  int rc;
+  if ((rc = peer_ptrs(recv_ptrs, P, &rp, "recv")) || (rc = peer_ptrs(meta_ptrs, P, &mp, "meta")))
+    return rc;
+  RB_CHECK_ARG(offsets && (n == 0 || (x && perm && aligned16(x))),
+               "moe_ep_scatter: null or unaligned pointer");
+  const int64_t want = (n + 7) / 8 + 1;
+  const int64_t cap_blocks = (int64_t)num_sms() * 16;
+  k_ep_scatter<<<(unsigned)(want < cap_blocks ? want : cap_blocks), 256, 0, as_stream(stream)>>>(
+      static_cast<const uint16_t*>(x), perm, offsets, n, k, (int)D, E / P, P, rank, cap, rp, mp);
+  RB_LAUNCH_CHECK();
+  return REMORA_B200_OK;
+}
+
+extern "C" int remora_b200_moe_ep_barrier(int32_t* flags, const uint64_t* flag_ptrs, int P,
+                                          int rank, int epoch, void* stream) {
+  clear_error();
+  RB_CHECK_ARG(P >= 1 && P <= 8 && rank >= 0 && rank < P && flags,
+               "moe_ep_barrier: bad arguments");
+  PeerPtrs fp = PeerPtrs{};
+  RB_CHECK_ARG(flag_ptrs, "moe_ep_barrier: null flag address list");
+  for (int i = 0; i < P; ++i) {
+    RB_CHECK_ARG(flag_ptrs[i] != 0 && (flag_ptrs[i] & 3u) == 0, "moe_ep_barrier: bad address");
+    fp.p[i] = flag_ptrs[i];
+  }
+  k_ep_barrier<<<1, 32, 0, as_stream(stream)>>>(flags, fp, P, rank, epoch);
+  RB_LAUNCH_CHECK();
+  return REMORA_B200_OK;
+}
+
+extern "C" int remora_b200_moe_ep_segments(const int32_t* meta, int P, int Epr, int64_t cap,
+                                           int32_t* seg, void* stream) {
+  clear_error();
+  RB_CHECK_ARG(meta && seg && P >= 1 && P <= 8 && Epr >= 1 && P * Epr <= GMaxE,
+               "moe_ep_segments: bad arguments");
+  const int S = P * Epr;
+  k_ep_segments<<<1, 32, 0, as_stream(stream)>>>(meta, P, Epr, cap, seg, seg + S, seg + 2 * S,
+                                                 seg + 3 * S, seg + 4 * S);
+  RB_LAUNCH_CHECK();
+  return REMORA_B200_OK;
+}
+
+// The local experts over the received rows: SwiGLU grouped GEMM into h
+// (same row layout as recv), then the down GEMM storing every output row
+// into its source rank's y (seg = the 5*S table of remora_b200_moe_ep_segments).
+extern "C" int remora_b200_moe_ep_experts_bf16(const void* recv, const void* wg, const void* wu,
+                                               const void* wd, void* h, const int32_t* seg,
+                                               int P, int Epr, int64_t cap, int64_t D,
+                                               int64_t F, const uint64_t* y_ptrs,
+                                               void* stream) {
+  clear_error();
+  RB_CHECK_ARG(P >= 1 && P <= 8 && Epr >= 1 && P * Epr <= GMaxE && seg,
+               "moe_ep_experts: bad arguments");
+  PeerPtrs yp;
+  int rc;
+  if ((rc = peer_ptrs(y_ptrs, P, &yp, "y"))) return rc;
+  const int S = P * Epr;
+  const int64_t rows = (int64_t)P * cap;
+  cudaStream_t st = as_stream(stream);
+  if ((rc = grouped_launch(true, recv, wg, wu, h, nullptr, rows, D, F, Epr, st, seg + 2 * S, S,
+                           seg, seg + S)))
+    return rc;
+  return grouped_launch(false, h, wd, nullptr, nullptr, nullptr, rows, F, D, Epr, st,
+                        seg + 2 * S, S, seg, seg + S, seg + 3 * S, seg + 4 * S, &yp);
+}

@@ -22,22 +22,33 @@
 namespace rb {
 namespace moe {
 
+struct PeerPtrs {
+  uint64_t p[8];  // device addresses of a buffer on up to 8 ranks
+};
+
 constexpr int GBM = 128, GBK = 64, GStages = 4, GGroupM = 16, GMaxE = 256;
 constexpr int GThreads = 192;
 constexpr uint32_t GABytes = GBM * GBK * 2;        // 16 KB
 constexpr uint32_t GBBytes = 256 * GBK * 2;        // 32 KB: 4 boxes of [64 K x 64 N]
 constexpr uint32_t GStageBytes = GABytes + GBBytes;
 constexpr uint32_t GBarOffset = GStages * GStageBytes;
-constexpr uint32_t GSmemBytes = GBarOffset + 256 + 3 * (GMaxE + 1) * 4 + 1024;
+constexpr uint32_t GSmemBytes = GBarOffset + 256 + 6 * (GMaxE + 1) * 4 + 1024;
 
 struct GroupShape {
   int K, N, E;
   int S;             // row segments (== E when segments are the experts)
   int tiles_n;       // N / (columns per tile)
   int num_kb;
-  const int32_t* offsets;     // [S+1] device: row segments
+  const int32_t* seg_start;   // [S] device: first row of segment q
+  const int32_t* seg_end;     // [S] device: one past its last row (seg_start + 1 for offsets)
   const int32_t* seg_expert;  // [S] device: expert of each segment, or null (segment s = expert s)
-  uint16_t* out;              // [rows, N] bf16
+  uint16_t* out;              // [rows, N] bf16 (local output when seg_dst_rank is null)
+  // Optional remote output: row g of segment q is stored at row
+  // seg_dst_row[q] + (g - seg_start[q]) of the [*, N] buffer dst.p[seg_dst_rank[q]]
+  // (another GPU's memory, plain stores over NVLink).
+  const int32_t* seg_dst_row;
+  const int32_t* seg_dst_rank;
+  PeerPtrs dst;
 };
 
 struct GSmem {
@@ -50,11 +61,12 @@ struct GSmem {
 };
 
 struct TileInfo {
-  int e, r0, r_end, n;
+  int e, r0, r_end, n, seg;
 };
 
-__device__ __forceinline__ TileInfo group_tile(const GroupShape& s, const int* mt, const int* off,
-                                               const int* sexp, int total_mt, int t) {
+__device__ __forceinline__ TileInfo group_tile(const GroupShape& s, const int* mt, const int* st,
+                                               const int* en, const int* sexp, int total_mt,
+                                               int t) {
   const int span = GGroupM * s.tiles_n;
   const int grp = t / span;
   const int first = grp * GGroupM;
@@ -69,8 +81,9 @@ __device__ __forceinline__ TileInfo group_tile(const GroupShape& s, const int* m
     if (mt[mid] <= g) lo = mid; else hi = mid;
   }
   ti.e = sexp[lo];
-  ti.r0 = off[lo] + (g - mt[lo]) * GBM;
-  ti.r_end = off[lo + 1];
+  ti.seg = lo;
+  ti.r0 = st[lo] + (g - mt[lo]) * GBM;
+  ti.r_end = en[lo];
   return ti;
 }
 
@@ -89,13 +102,19 @@ __global__ void __launch_bounds__(GThreads, 1)
                                              ~uintptr_t(1023));
   GSmem* sm = reinterpret_cast<GSmem*>(smem + GBarOffset);
   int* s_mt = reinterpret_cast<int*>(smem + GBarOffset + 256);
-  int* s_off = s_mt + (GMaxE + 1);
-  int* s_exp = s_off + (GMaxE + 1);
+  int* s_st = s_mt + (GMaxE + 1);
+  int* s_en = s_st + (GMaxE + 1);
+  int* s_exp = s_en + (GMaxE + 1);
+  int* s_drow = s_exp + (GMaxE + 1);
+  int* s_drank = s_drow + (GMaxE + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   for (int i = threadIdx.x; i <= s.S; i += blockDim.x) {
-    s_off[i] = s.offsets[i];
     if (i < s.S) {
+      s_st[i] = s.seg_start[i];
+      s_en[i] = s.seg_end[i];
+      s_drow[i] = s.seg_dst_row ? s.seg_dst_row[i] : 0;
+      s_drank[i] = s.seg_dst_rank ? s.seg_dst_rank[i] : 0;
       const int e = s.seg_expert ? s.seg_expert[i] : i;
       s_exp[i] = (e >= 0 && e < s.E) ? e : 0;
       if (e < 0 || e >= s.E) atomicExch(&g_device_error, 2);
@@ -107,7 +126,7 @@ __global__ void __launch_bounds__(GThreads, 1)
     int mt = 0;
     for (int q = 0; q < s.S; ++q) {
       s_mt[q] = mt;
-      mt += (s_off[q + 1] - s_off[q] + GBM - 1) / GBM;
+      mt += max(s_en[q] - s_st[q], 0) / GBM + ((max(s_en[q] - s_st[q], 0) % GBM) ? 1 : 0);
     }
     s_mt[s.S] = mt;
     for (int i = 0; i < GStages; ++i) {
@@ -143,7 +162,7 @@ __global__ void __launch_bounds__(GThreads, 1)
       int stage = 0, issued = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
-        const TileInfo ti = group_tile(s, s_mt, s_off, s_exp, total_mt, t);
+        const TileInfo ti = group_tile(s, s_mt, s_st, s_en, s_exp, total_mt, t);
         const int n0 = ti.n * kColsPerTile;
         for (int kb = 0; kb < s.num_kb; ++kb) {
           if (!mbar_wait(&sm->empty[stage], phase ^ 1)) { *abort_flag = 1; break; }
@@ -220,14 +239,19 @@ __global__ void __launch_bounds__(GThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const TileInfo ti = group_tile(s, s_mt, s_off, s_exp, total_mt, t);
+      const TileInfo ti = group_tile(s, s_mt, s_st, s_en, s_exp, total_mt, t);
       bool got = !*abort_flag && mbar_wait(&sm->tmem_full[acc], acc_phase);
       if (!__all_sync(0xffffffffu, got)) { *abort_flag = 1; break; }
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(lg * 32) << 16) + acc * 256;
       const int grow = ti.r0 + row;
       const bool valid = grow < ti.r_end;
-      uint16_t* dst = s.out + (int64_t)grow * s.N + ti.n * kColsPerTile;
+      uint16_t* dst =
+          (s.seg_dst_rank
+               ? reinterpret_cast<uint16_t*>(s.dst.p[s_drank[ti.seg]]) +
+                     (int64_t)(s_drow[ti.seg] + (grow - s_st[ti.seg])) * s.N
+               : s.out + (int64_t)grow * s.N) +
+          ti.n * kColsPerTile;
       constexpr int kChunks = kColsPerTile / 32;
 #pragma unroll 1
       for (int c = 0; c < kChunks; ++c) {

@@ -92,7 +92,10 @@ int gather_launch(const void* x, const int32_t* perm, int64_t rows, int k, int64
 // SwiGLU form) [E, K, N]; out [rows, N].  offsets [E+1] on the device.
 int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, void* out,
                    const int32_t* offsets, int64_t rows, int64_t K, int64_t N, int E,
-                   cudaStream_t st, const int32_t* seg_expert = nullptr, int n_seg = -1) {
+                   cudaStream_t st, const int32_t* seg_expert = nullptr, int n_seg = -1,
+                   const int32_t* seg_start = nullptr, const int32_t* seg_end = nullptr,
+                   const int32_t* dst_row = nullptr, const int32_t* dst_rank = nullptr,
+                   const PeerPtrs* dst = nullptr) {
   const int cols = swiglu ? 128 : 256;
   const int S = n_seg < 0 ? E : n_seg;
   RB_CHECK_ARG(E >= 1 && E <= GMaxE, "grouped_gemm: E=%d unsupported (1..%d)", E, GMaxE);
@@ -103,8 +106,11 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   RB_CHECK_ARG(rows < (1ll << 31) && K < (1ll << 31) && N < (1ll << 31),
                "grouped_gemm: sizes exceed 2^31");
   if (rows == 0) return REMORA_B200_OK;
-  RB_CHECK_ARG(a && b0 && out && offsets && (!swiglu || b1), "grouped_gemm: null pointer");
-  RB_CHECK_ARG(aligned16(a) && aligned16(b0) && aligned16(out) && (!swiglu || aligned16(b1)),
+  RB_CHECK_ARG(a && b0 && (out || dst) && (offsets || (seg_start && seg_end)) &&
+                   (!swiglu || b1),
+               "grouped_gemm: null pointer");
+  RB_CHECK_ARG(aligned16(a) && aligned16(b0) && (!out || aligned16(out)) &&
+                   (!swiglu || aligned16(b1)),
                "grouped_gemm: pointers must be 16-byte aligned");
   CUtensorMap tA, tB0, tB1;
   int rc;
@@ -133,7 +139,11 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   sh.seg_expert = seg_expert;
   sh.tiles_n = (int)((N + cols - 1) / cols);
   sh.num_kb = (int)((K + GBK - 1) / GBK);
-  sh.offsets = offsets;
+  sh.seg_start = seg_start ? seg_start : offsets;
+  sh.seg_end = seg_end ? seg_end : offsets + 1;
+  sh.seg_dst_row = dst ? dst_row : nullptr;
+  sh.seg_dst_rank = dst ? dst_rank : nullptr;
+  sh.dst = dst ? *dst : PeerPtrs{};
   sh.out = static_cast<uint16_t*>(out);
   // upper bound of the tile count: sum over experts of ceil(n_e / 128)
   const int64_t max_tiles = (rows / GBM + S) * (int64_t)sh.tiles_n;

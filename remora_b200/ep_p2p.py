@@ -1,0 +1,106 @@
+"""Expert-parallel MoE layer with the token exchange done by the library's
+own kernels over NVLink peer memory (no NCCL in the layer, no host round
+trip for split sizes).
+
+Buffers every rank can address come from torch symmetric memory, allocated
+once per ``PeerEP`` (sized for the worst case: one rank may route all of
+its T_local*k rows to one peer).  One layer on rank r:
+
+  router + top-k, dispatch over all E experts              (kernels)
+  scatter: row p -> region r of rank (expert // Epr)'s recv (kernel, NVLink)
+  barrier                                                   (kernel, bounded)
+  segments from meta; SwiGLU grouped GEMM; down grouped GEMM whose epilogue
+  stores each output row into its source rank's y           (kernels, NVLink)
+  barrier                                                   (kernel, bounded)
+  combine of y in slot order                                (kernel)
+
+The two barriers also order consecutive layers: a rank writes a peer's
+recv / meta / y only after every rank has finished reading them.  Results
+are bit-identical to the single-GPU layer (each row's expert output depends
+only on that row and its expert's weights).
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+
+def _align(n: int, a: int = 256) -> int:
+    return (n + a - 1) // a * a
+
+
+class PeerEP:
+    def __init__(self, T_local: int, D: int, F: int, E: int, k: int, group=None, device=None):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        import remora_b200 as rb
+
+        self.rb = rb
+        self.group = group
+        self.P = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if E % self.P or self.P > 8:
+            raise ValueError(f"{E} experts over {self.P} ranks (at most 8) do not split")
+        self.T, self.D, self.F, self.E, self.k = T_local, D, F, E, k
+        self.Epr = E // self.P
+        self.cap = T_local * k
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        P, cap = self.P, self.cap
+        self.off_flags = 0
+        self.off_meta = _align(P * 4)
+        self.off_recv = self.off_meta + _align(P * (self.Epr + 1) * 4)
+        self.off_y = self.off_recv + _align(P * cap * D * 2)
+        total = self.off_y + _align(cap * D * 2)
+        self.buf = symm_mem.empty(total, dtype=torch.uint8, device=self.device)
+        self.buf.zero_()
+        torch.cuda.synchronize(self.device)
+        gname = group.group_name if group is not None else dist.group.WORLD.group_name
+        if hasattr(symm_mem, "enable_symm_mem_for_group"):
+            try:
+                symm_mem.enable_symm_mem_for_group(gname)
+            except Exception:
+                pass
+        self.hdl = symm_mem.rendezvous(self.buf, gname)
+        base = list(self.hdl.buffer_ptrs)
+        arr = lambda off: (ctypes.c_uint64 * P)(*[b + off for b in base])
+        self.flag_ptrs, self.meta_ptrs = arr(self.off_flags), arr(self.off_meta)
+        self.recv_ptrs, self.y_ptrs = arr(self.off_recv), arr(self.off_y)
+        view = lambda off, n, dt: self.buf[off:off + n * torch.tensor([], dtype=dt).element_size()].view(dt)
+        self.flags = view(self.off_flags, P, torch.int32)
+        self.meta = view(self.off_meta, P * (self.Epr + 1), torch.int32)
+        self.recv = view(self.off_recv, P * cap * D, torch.bfloat16).view(P * cap, D)
+        self.y = view(self.off_y, cap * D, torch.bfloat16).view(cap, D)
+        self.h = torch.empty(P * cap, F, dtype=torch.bfloat16, device=self.device)
+        self.seg = torch.empty(5 * P * self.Epr, dtype=torch.int32, device=self.device)
+        self.epoch = 0
+        dist.barrier(group)
+
+    def _barrier(self, stream):
+        self.epoch += 1
+        self.rb._check(self.rb.lib().remora_b200_moe_ep_barrier(
+            self.flags.data_ptr(), self.flag_ptrs, self.P, self.rank, self.epoch, stream))
+
+    def forward(self, x, wr, wg_local, wu_local, wd_local):
+        """x [T_local, D]; wr [D, E]; this rank's experts wg/wu [Epr, D, F],
+        wd [Epr, F, D].  Returns out [T_local, D] bf16."""
+        rb, L = self.rb, self.rb.lib()
+        if x.shape != (self.T, self.D) or wg_local.shape[0] != self.Epr:
+            raise ValueError("shapes differ from the ones this PeerEP was built for")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        idx, w = rb.moe_router_topk(x, wr, self.k)
+        counts, offsets, perm, inv = rb.moe_dispatch(idx, self.E)
+        rb._check(L.remora_b200_moe_ep_scatter_bf16(
+            x.data_ptr(), perm.data_ptr(), offsets.data_ptr(), self.cap, self.k, self.D, self.E,
+            self.P, self.rank, self.cap, self.recv_ptrs, self.meta_ptrs, stream))
+        self._barrier(stream)
+        rb._check(L.remora_b200_moe_ep_segments(self.meta.data_ptr(), self.P, self.Epr, self.cap,
+                                                self.seg.data_ptr(), stream))
+        rb._check(L.remora_b200_moe_ep_experts_bf16(
+            self.recv.data_ptr(), wg_local.contiguous().data_ptr(),
+            wu_local.contiguous().data_ptr(), wd_local.contiguous().data_ptr(),
+            self.h.data_ptr(), self.seg.data_ptr(), self.P, self.Epr, self.cap, self.D, self.F,
+            self.y_ptrs, stream))
+        self._barrier(stream)
+        return rb.moe_combine(self.y, inv, w)

@@ -24,7 +24,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, cfg, outdir):
+def _worker(rank, world, port, cfg, outdir, mode="nccl"):
     sys.path.insert(0, ROOT)
     import remora_b200 as rb
     from remora_b200.ep import moe_ep_forward
@@ -46,21 +46,29 @@ def _worker(rank, world, port, cfg, outdir):
                       (wd, 34, 0.02)):
         rb.fill_normal(t, rb.stream_key(s), 0.0, sig)
     tl, Epr = T // world, E // world
-    out = moe_ep_forward(x[rank * tl:(rank + 1) * tl].contiguous(), wr,
-                         wg[rank * Epr:(rank + 1) * Epr].contiguous(),
-                         wu[rank * Epr:(rank + 1) * Epr].contiguous(),
-                         wd[rank * Epr:(rank + 1) * Epr].contiguous(), k, E)
-    rb.synchronize_and_check(dev)
+    xl = x[rank * tl:(rank + 1) * tl].contiguous()
+    wl = [w_[rank * Epr:(rank + 1) * Epr].contiguous() for w_ in (wg, wu, wd)]
     ref = rb.moe_layer(x, wr, wg, wu, wd, k)[rank * tl:(rank + 1) * tl]
-    same = torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    same = True
+    if mode == "nccl":
+        outs = [moe_ep_forward(xl, wr, *wl, k, E)]
+    else:
+        from remora_b200.ep_p2p import PeerEP
+
+        ep = PeerEP(tl, D, F, E, k)
+        outs = [ep.forward(xl, wr, *wl).clone() for _ in range(3)]  # consecutive layers
+    rb.synchronize_and_check(dev)
+    for out in outs:
+        same = same and torch.equal(out.view(torch.int16), ref.view(torch.int16))
     with open(os.path.join(outdir, f"r{rank}.txt"), "w") as f:
         f.write("same" if same else "differ")
     dist.barrier()
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("mode", ["nccl", "p2p"])
 @pytest.mark.parametrize("cfg", [(4096, 512, 256, 16, 4), (8192, 2048, 1536, 64, 8)])
-def test_ep_matches_single_gpu_layer(rb, tmp_path, cfg):
+def test_ep_matches_single_gpu_layer(rb, tmp_path, cfg, mode):
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
@@ -68,7 +76,7 @@ def test_ep_matches_single_gpu_layer(rb, tmp_path, cfg):
         world //= 2
     port = _free_port()
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, str(tmp_path)))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, str(tmp_path), mode))
              for r in range(world)]
     for p in procs:
         p.start()
