@@ -32,7 +32,8 @@ constexpr uint32_t GABytes = GBM * GBK * 2;        // 16 KB
 constexpr uint32_t GBBytes = 256 * GBK * 2;        // 32 KB: 4 boxes of [64 K x 64 N]
 constexpr uint32_t GStageBytes = GABytes + GBBytes;
 constexpr uint32_t GBarOffset = GStages * GStageBytes;
-constexpr uint32_t GSmemBytes = GBarOffset + 256 + 6 * (GMaxE + 1) * 4 + 1024;
+constexpr uint32_t GEpiOffset = GBarOffset + ((256 + 6 * (GMaxE + 1) * 4 + 1023) & ~1023u);
+constexpr uint32_t GSmemBytes = GEpiOffset + 4 * 32 * 128 + 1024;
 
 struct GroupShape {
   int K, N, E;
@@ -107,6 +108,8 @@ __global__ void __launch_bounds__(GThreads, 1)
   int* s_exp = s_en + (GMaxE + 1);
   int* s_drow = s_exp + (GMaxE + 1);
   int* s_drank = s_drow + (GMaxE + 1);
+  // per epilogue warp: one [32 rows][128 B] staging tile, 1024-byte aligned
+  uint8_t* epi_stage_base = smem + GEpiOffset;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   for (int i = threadIdx.x; i <= s.S; i += blockDim.x) {
@@ -235,7 +238,7 @@ __global__ void __launch_bounds__(GThreads, 1)
     }
   } else {
     const int lg = warp & 3;
-    const int row = lg * 32 + lane;
+    uint8_t* epi_stage = epi_stage_base + (warp - 2) * 32 * 128;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
@@ -244,46 +247,74 @@ __global__ void __launch_bounds__(GThreads, 1)
       if (!__all_sync(0xffffffffu, got)) { *abort_flag = 1; break; }
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(lg * 32) << 16) + acc * 256;
-      const int grow = ti.r0 + row;
-      const bool valid = grow < ti.r_end;
-      uint16_t* dst =
-          (s.seg_dst_rank
-               ? reinterpret_cast<uint16_t*>(s.dst.p[s_drank[ti.seg]]) +
-                     (int64_t)(s_drow[ti.seg] + (grow - s_st[ti.seg])) * s.N
-               : s.out + (int64_t)grow * s.N) +
-          ti.n * kColsPerTile;
-      constexpr int kChunks = kColsPerTile / 32;
+      // Output rows of this warp: tile rows lg*32 .. lg*32+31.  Each 64-column
+      // block is packed to bf16, staged in a 128-byte-swizzled [32][64] smem
+      // tile, then copied out with 8 lanes per row: every store instruction
+      // writes four full 128-byte row segments (local HBM, or a peer GPU's
+      // memory over NVLink when the segment names a destination rank).
+      const int n_base = ti.n * kColsPerTile;
+      const int row_base = ti.r0 + lg * 32;
+      uint16_t* seg_base =
+          s.seg_dst_rank ? reinterpret_cast<uint16_t*>(s.dst.p[s_drank[ti.seg]]) : s.out;
+      const int64_t row_shift = s.seg_dst_rank ? (int64_t)s_drow[ti.seg] - s_st[ti.seg] : 0;
+      const uint32_t stage = smem_u32(epi_stage);
+      constexpr int kBlocks = kColsPerTile / 64;
 #pragma unroll 1
-      for (int c = 0; c < kChunks; ++c) {
-        uint32_t pk[16];
+      for (int c = 0; c < kBlocks; ++c) {
+        uint32_t pk[32];
         if (kSwiGLU) {
-          uint32_t g[32], u[32];
-          tmem_ld32(t_row + c * 32, g);
-          tmem_ld32(t_row + 128 + c * 32, u);
-          tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pk[i] = pack_bf16x2(silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i])),
-                                silu_mul(__uint_as_float(g[2 * i + 1]),
-                                         __uint_as_float(u[2 * i + 1])));
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t g[32], u[32];
+            tmem_ld32(t_row + c * 64 + h2 * 32, g);
+            tmem_ld32(t_row + 128 + c * 64 + h2 * 32, u);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pk[h2 * 16 + i] =
+                  pack_bf16x2(silu_mul(__uint_as_float(g[2 * i]), __uint_as_float(u[2 * i])),
+                              silu_mul(__uint_as_float(g[2 * i + 1]),
+                                       __uint_as_float(u[2 * i + 1])));
+          }
         } else {
-          uint32_t v[32];
-          tmem_ld32(t_row + c * 32, v);
-          tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pk[i] = pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+          for (int h2 = 0; h2 < 2; ++h2) {
+            uint32_t v[32];
+            tmem_ld32(t_row + c * 64 + h2 * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              pk[h2 * 16 + i] =
+                  pack_bf16x2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+          }
         }
-        if (c == kChunks - 1) {
+        if (c == kBlocks - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&sm->tmem_empty[acc]);
         }
-        if (valid && ti.n * kColsPerTile + c * 32 < s.N) {  // N % 32 == 0
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+        __syncwarp();  // the previous block's copy-out has read the stage
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        for (int j = 0; j < 8; ++j)
+          st_shared_v4(stage + lane * 128 + ((j ^ (lane & 7)) << 4), pk[4 * j], pk[4 * j + 1],
+                       pk[4 * j + 2], pk[4 * j + 3]);
+        __syncwarp();
+        const int col0 = n_base + c * 64;
+        if (col0 < s.N) {  // N % 32 == 0: a block is either in range or half in range
+          const int j = lane & 7;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int r = i * 4 + (lane >> 3);
+            const int grow = row_base + r;
+            if (grow < ti.r_end && col0 + j * 8 < s.N) {
+              uint4 v;
+              asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                           : "r"(stage + r * 128 + ((j ^ (r & 7)) << 4)));
+              *reinterpret_cast<uint4*>(seg_base + (grow + row_shift) * (int64_t)s.N + col0 +
+                                        j * 8) = v;
+            }
+          }
         }
       }
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }

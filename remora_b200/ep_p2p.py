@@ -75,6 +75,8 @@ class PeerEP:
         self.h = torch.empty(P * cap, F, dtype=torch.bfloat16, device=self.device)
         self.seg = torch.empty(5 * P * self.Epr, dtype=torch.int32, device=self.device)
         self.epoch = 0
+        self.profile = False   # when True, forward() records per-phase CUDA events
+        self.phase_ms = {}
         dist.barrier(group)
 
     def _barrier(self, stream):
@@ -88,13 +90,26 @@ class PeerEP:
         rb, L = self.rb, self.rb.lib()
         if x.shape != (self.T, self.D) or wg_local.shape[0] != self.Epr:
             raise ValueError("shapes differ from the ones this PeerEP was built for")
-        stream = torch.cuda.current_stream(self.device).cuda_stream
+        cs = torch.cuda.current_stream(self.device)
+        stream = cs.cuda_stream
+        marks = []
+
+        def mark(name):
+            if self.profile:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(cs)
+                marks.append((name, ev))
+
+        mark("start")
         idx, w = rb.moe_router_topk(x, wr, self.k)
         counts, offsets, perm, inv = rb.moe_dispatch(idx, self.E)
+        mark("route+dispatch")
         rb._check(L.remora_b200_moe_ep_scatter_bf16(
             x.data_ptr(), perm.data_ptr(), offsets.data_ptr(), self.cap, self.k, self.D, self.E,
             self.P, self.rank, self.cap, self.recv_ptrs, self.meta_ptrs, stream))
+        mark("scatter")
         self._barrier(stream)
+        mark("barrier1")
         rb._check(L.remora_b200_moe_ep_segments(self.meta.data_ptr(), self.P, self.Epr, self.cap,
                                                 self.seg.data_ptr(), stream))
         rb._check(L.remora_b200_moe_ep_experts_bf16(
@@ -102,5 +117,12 @@ class PeerEP:
             wu_local.contiguous().data_ptr(), wd_local.contiguous().data_ptr(),
             self.h.data_ptr(), self.seg.data_ptr(), self.P, self.Epr, self.cap, self.D, self.F,
             self.y_ptrs, stream))
+        mark("experts")
         self._barrier(stream)
-        return rb.moe_combine(self.y, inv, w)
+        mark("barrier2")
+        out = rb.moe_combine(self.y, inv, w)
+        mark("combine")
+        if self.profile:
+            marks[-1][1].synchronize()
+            self.phase_ms = {b[0]: a[1].elapsed_time(b[1]) for a, b in zip(marks, marks[1:])}
+        return out
