@@ -44,7 +44,20 @@ __global__ void k_ep_scatter(const uint16_t* __restrict__ x, const int32_t* __re
     const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(perm[p] / k) * D);
     uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(recv.p[q]) +
                                           ((int64_t)rank * cap + i) * D);
-    for (int c = lane; c < D / 8; c += 32) dst[c] = __ldg(src + c);
+    // up to 8 pieces of 16 bytes in flight per lane before they are stored
+    for (int c0 = 0; c0 < D / 8; c0 += 8 * 32) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < D / 8) v[u] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < D / 8) dst[c] = v[u];
+      }
+    }
   }
 }
 

@@ -19,10 +19,14 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
   RB_CHECK_ARG(x && wr && idx && w, "router: null pointer");
   RB_CHECK_ARG(aligned16(x), "router: x must be 16-byte aligned");
   RB_CHECK_ARG(T < (1ll << 31) && D < (1ll << 31), "router: sizes exceed 2^31");
-  // expert groups of 8 per token (power of two) and tokens per thread
+  // expert groups of 8 per token (power of two) and tokens per thread: as
+  // many as keep at least two blocks per SM (small T gets more blocks)
   int ng = 1;
   while (ng * 8 < E) ng *= 2;
-  const int rt = ng >= 8 ? 4 : (ng >= 2 ? 2 : 1);
+  int rt = ng >= 8 ? 4 : (ng >= 2 ? 2 : 1);
+  while (rt > 1 && (T + (kRouterThreads / ng) * rt - 1) / ((kRouterThreads / ng) * rt) <
+                       2 * (int64_t)num_sms())
+    rt /= 2;
   const int tpb = (kRouterThreads / ng) * rt;
   const size_t smem = ((size_t)tpb + (size_t)ng * 8) * kRowPadF * 4;
   const int64_t grid = (T + tpb - 1) / tpb;
@@ -35,12 +39,20 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
     return REMORA_B200_OK;
   };
   int rc;
-  switch (ng) {
-    case 1: rc = launch(k_router_topk<1, 1>); break;
-    case 2: rc = launch(k_router_topk<2, 2>); break;
-    case 4: rc = launch(k_router_topk<2, 4>); break;
-    case 8: rc = launch(k_router_topk<4, 8>); break;
-    case 16: rc = launch(k_router_topk<4, 16>); break;
+  switch (ng * 8 + rt) {
+    case 1 * 8 + 1: rc = launch(k_router_topk<1, 1>); break;
+    case 2 * 8 + 1: rc = launch(k_router_topk<1, 2>); break;
+    case 2 * 8 + 2: rc = launch(k_router_topk<2, 2>); break;
+    case 4 * 8 + 1: rc = launch(k_router_topk<1, 4>); break;
+    case 4 * 8 + 2: rc = launch(k_router_topk<2, 4>); break;
+    case 8 * 8 + 1: rc = launch(k_router_topk<1, 8>); break;
+    case 8 * 8 + 2: rc = launch(k_router_topk<2, 8>); break;
+    case 8 * 8 + 4: rc = launch(k_router_topk<4, 8>); break;
+    case 16 * 8 + 1: rc = launch(k_router_topk<1, 16>); break;
+    case 16 * 8 + 2: rc = launch(k_router_topk<2, 16>); break;
+    case 16 * 8 + 4: rc = launch(k_router_topk<4, 16>); break;
+    case 32 * 8 + 1: rc = launch(k_router_topk<1, 32>); break;
+    case 32 * 8 + 2: rc = launch(k_router_topk<2, 32>); break;
     default: rc = launch(k_router_topk<4, 32>); break;
   }
   if (rc) return rc;
