@@ -147,6 +147,19 @@ def max_over_ranks(v: float, world: int) -> float:
     return float(t.item())
 
 
+def all_ranks(v: float, world: int) -> list:
+    """Every rank's value (rank order), gathered over the process group."""
+    if world == 1:
+        return [v]
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
+
+
 def barrier(world: int):
     if world > 1:
         import torch.distributed as dist
@@ -515,7 +528,9 @@ def bench_moe_ep(args, world, rank, local):
         ev1.record(stream)
         torch.cuda.synchronize(dev)
     barrier(world)
-    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    rank_ms = all_ranks(ms_local, world)
+    ms = max(rank_ms)
     xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
     oh = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
     xh.copy_(x)
@@ -541,7 +556,8 @@ def bench_moe_ep(args, world, rank, local):
                    "parallelism": (f"EP{world} ({'NVLink peer-memory scatter/combine' if pep else 'NCCL all-to-all'})"
                                    if world > 1 else "single GPU"),
                    "ep_chunks": args.ep_chunks or "default",
-                   "expert_flop_per_step": flop},
+                   "expert_flop_per_step": flop,
+                   "rank_ms": [round(v, 4) for v in rank_ms]},
         "roofline": {"bound": "tensor", "achieved": per_gpu_tf, "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": per_gpu_tf / peaks["bf16_tflops"],
                      "peak_source": src, "traffic": None,
