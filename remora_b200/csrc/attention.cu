@@ -227,9 +227,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < BKV; ++c)
           r[c] = (kv0 + c >= lim) ? 0xff800000u : r[c];  // -inf past the limit
       }
-      float mx = __uint_as_float(r[0]);
+      // row max as 8 independent chains (a single 127-long fmaxf chain is
+      // latency-bound with two softmax warps per scheduler)
+      float pm[8];
 #pragma unroll
-      for (int c = 1; c < BKV; ++c) mx = fmaxf(mx, __uint_as_float(r[c]));
+      for (int i = 0; i < 8; ++i) pm[i] = __uint_as_float(r[i]);
+#pragma unroll
+      for (int c = 8; c < BKV; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(r[c]));
+      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
       const float mt = mx * p.sl2;
       // Raise the running max only when it grows by more than 8 (log2 units).
       const bool raise = mt > m + 8.0f;
@@ -242,14 +248,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float mu = (m == -INFINITY) ? 0.0f : m;
       // P packs two bf16 per 32-bit column (even element in the low half);
       // r[c/2] is written only after r[c] and r[c+1] have been read.
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 partial row sums
 #pragma unroll
       for (int c = 0; c < BKV; c += 2) {
         const float a = ex2(fmaf(__uint_as_float(r[c]), p.sl2, -mu));
         const float b = ex2(fmaf(__uint_as_float(r[c + 1]), p.sl2, -mu));
-        l += a;
-        l += b;
+        ps[(c >> 1) & 7] += a + b;
         r[c >> 1] = pack_bf16x2(a, b);
       }
+      l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
 #pragma unroll
       for (int c = 0; c < 4; ++c)
         tmem_st16(t_s + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&r[c * 16]));
