@@ -501,16 +501,16 @@ def bench_moe_ep(args, world, rank, local):
            if world == 1 else None)
 
     pep = None
-    if world > 1 and args.ep_mode == "p2p":
+    if world > 1 and args.ep_mode in ("p2p", "p2p-split"):
         from remora_b200.ep_p2p import PeerEP
 
-        pep = PeerEP(tl, D, F, E, k, device=dev)
+        pep = PeerEP(tl, D, F, E, k, device=dev, fused=args.ep_mode == "p2p")
 
     def step():
         if world == 1:
             rb.moe_layer(x, wr, wg, wu, wd, k, out=out, workspace=lws)
         elif pep is not None:
-            out.copy_(pep.forward(x, wr, wg, wu, wd))
+            pep.forward(x, wr, wg, wu, wd, out=out)
         else:
             out.copy_(moe_ep_forward(x, wr, wg, wu, wd, k, E, chunks=args.ep_chunks or None))
 
@@ -553,7 +553,7 @@ def bench_moe_ep(args, world, rank, local):
         "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, bf16)",
         "config": {"workload": f"expert-parallel MoE config 5: T={T} D={D} F={F} E={E} top-{k}, "
                                f"{Epr} experts and {tl} tokens per GPU",
-                   "parallelism": (f"EP{world} ({'NVLink peer-memory scatter/combine' if pep else 'NCCL all-to-all'})"
+                   "parallelism": (f"EP{world} ({EP_MODES[args.ep_mode]})"
                                    if world > 1 else "single GPU"),
                    "ep_chunks": args.ep_chunks or "default",
                    "expert_flop_per_step": flop,
@@ -565,8 +565,18 @@ def bench_moe_ep(args, world, rank, local):
         "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s",
                 "h2d_bytes_per_step": x.numel() * 2 * world,
                 "d2h_bytes_per_step": out.numel() * 2 * world, "ms_per_step": e2e_ms},
-        "gpu_launches": 8 * args.steps, "clocks": clk.summary(),
+        "gpu_launches": (EP_LAUNCHES[args.ep_mode] if world > 1 else 8) * args.steps,
+        "clocks": clk.summary(),
     }
+
+
+# kernels of one EP layer: router 1, dispatch 3, then (fused) meta, dispatch+SwiGLU, down,
+# barrier, combine; (split) scatter, barrier, segments, SwiGLU, down, barrier, combine
+EP_LAUNCHES = {"p2p": 9, "p2p-split": 11, "nccl": 9}
+EP_MODES = {"p2p": "NVLink peer memory: scatter fused into the SwiGLU GEMM, down-GEMM epilogue "
+                   "stores to the source ranks",
+            "p2p-split": "NVLink peer memory: scatter kernel, barrier, GEMMs",
+            "nccl": "NCCL all-to-all"}
 
 
 def bench_attention(args, world, rank, local):
@@ -732,7 +742,7 @@ def main():
     ap.add_argument("--workload", choices=["gemm", "elementwise", "moe", "moe_ep", "attention"],
                     default="gemm")
     ap.add_argument("--moe-config", choices=sorted(MOE_CONFIGS), default="4")
-    ap.add_argument("--ep-mode", choices=["p2p", "nccl"], default="p2p",
+    ap.add_argument("--ep-mode", choices=["p2p", "p2p-split", "nccl"], default="p2p",
                     help="moe_ep: token exchange by the library's peer-memory kernels or NCCL")
     ap.add_argument("--ep-chunks", type=int, default=0,
                     help="moe_ep: token pieces per layer for comm/compute overlap (0 = default)")

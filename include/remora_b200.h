@@ -295,6 +295,44 @@ int remora_b200_moe_ep_experts_bf16(const void* recv, const void* wg, const void
                                     int64_t cap, int64_t D, int64_t F, const uint64_t* y_ptrs,
                                     void* stream);
 
+/* Fused form of the exchange (three calls per layer instead of scatter,
+ * barrier, segments, experts).  It needs, beside the buffers above, a
+ * peer-addressable ready[E] int32 (slot s*(E/P)+e: source s, local expert
+ * e; zero-initialised once) and a local done[E] int32 scratch.
+ *
+ * Step 1: publishes this rank's per-expert row counts in every peer's meta,
+ * zeroes done, barriers on `epoch` (as remora_b200_moe_ep_barrier) and
+ * builds the 5*E segment table from the received meta with the sources in
+ * delivery order rank, rank-1, ... (start, end, local expert, destination
+ * row, source rank). */
+int remora_b200_moe_ep_meta(const int32_t* offsets, int P, int E, int rank, int64_t cap,
+                            const uint64_t* meta_ptrs, const int32_t* meta_local,
+                            int32_t* flags, const uint64_t* flag_ptrs, int epoch,
+                            int32_t* done, int32_t* seg, void* stream);
+
+/* Step 2: one cooperative kernel (one CTA per SM) whose extra warps copy
+ * this rank's n dispatched rows into region `rank` of their owners' recv
+ * (destinations in the order rank, rank+1, ...) and publish `epoch` (the
+ * layer count, increasing) in the owner's ready slot of an expert once all
+ * of the expert's rows are stored, while the tcgen05 pipeline runs the
+ * SwiGLU grouped GEMM over the received segments (recv_local -> h
+ * [P*cap, F]); a segment's first tile waits, bounded, for its ready slot.
+ * REMORA_B200_EP_SCATTER_WARPS (2, 4 or 8; default 2) sets the copy warps
+ * per CTA. */
+int remora_b200_moe_ep_dispatch_swiglu_bf16(
+    const void* x, const int32_t* perm, const int32_t* offsets, int64_t n, int k, int64_t D,
+    int64_t F, int E, int P, int rank, int64_t cap, const uint64_t* recv_ptrs,
+    const uint64_t* ready_ptrs, const int32_t* ready_local, int32_t* done, int epoch,
+    const void* recv_local, const void* wg, const void* wu, void* h, const int32_t* seg,
+    void* stream);
+
+/* Step 3: the down grouped GEMM over the same segments, each output row
+ * stored into its source rank's y (followed by a barrier and the local
+ * remora_b200_moe_combine_bf16). */
+int remora_b200_moe_ep_down_bf16(const void* h, const void* wd, const int32_t* seg, int P,
+                                 int E, int64_t cap, int64_t F, int64_t D,
+                                 const uint64_t* y_ptrs, void* stream);
+
 /* ------------------------------------------------------------------------
  * Seeded input generator (device side of the counter-based generator the
  * tests and benchmarks use; one stream key per tensor)

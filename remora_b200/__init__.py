@@ -86,6 +86,10 @@ _SIGNATURES = {
     "remora_b200_moe_ep_barrier": ([P, P, I, I, I, P], I),
     "remora_b200_moe_ep_segments": ([P, I, I, I64, P, P], I),
     "remora_b200_moe_ep_experts_bf16": ([P, P, P, P, P, P, I, I, I64, I64, I64, P, P], I),
+    "remora_b200_moe_ep_meta": ([P, I, I, I, I64, P, P, P, P, I, P, P, P], I),
+    "remora_b200_moe_ep_dispatch_swiglu_bf16": ([P, P, P, I64, I, I64, I64, I, I, I, I64, P, P,
+                                                 P, P, I, P, P, P, P, P, P], I),
+    "remora_b200_moe_ep_down_bf16": ([P, P, P, I, I, I64, I64, I64, P, P], I),
     "remora_b200_device_status": ([], I),
     "remora_b200_fill_normal": ([P, I64, I, U64, D, D, P], I),
     "remora_b200_fill_uniform": ([P, I64, I, U64, D, D, P], I),
@@ -356,12 +360,16 @@ def grouped_gemm_segments(a, w, seg_offsets, seg_expert) -> torch.Tensor:
     return y
 
 
-def moe_combine(y: torch.Tensor, inv: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+def moe_combine(y: torch.Tensor, inv: torch.Tensor, w: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
     _dev(y, inv, w)
     _i32(inv)
     T, k = w.shape
     D = y.shape[1]
-    out = torch.empty((T, D), dtype=torch.bfloat16, device=y.device)
+    if out is None:
+        out = torch.empty((T, D), dtype=torch.bfloat16, device=y.device)
+    elif out.shape != (T, D) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise ValueError("moe_combine: out must be a contiguous bf16 [T, D] tensor")
     _check(lib().remora_b200_moe_combine_bf16(y.contiguous().data_ptr(), inv.data_ptr(),
                                               w.contiguous().data_ptr(), T, k, D, out.data_ptr(),
                                               _stream(y)))

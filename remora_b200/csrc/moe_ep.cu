@@ -109,6 +109,68 @@ __global__ void k_ep_segments(const int32_t* __restrict__ meta, int P, int Epr, 
   }
 }
 
+// Metadata exchange of the fused path, one warp: publish this rank's
+// per-expert row counts (and its base row) in region `rank` of every peer's
+// meta, zero the scatter completion counters done[E], barrier on `epoch`, then build
+// the segment table from the received meta with the sources in the order
+// the fused scatter delivers them: rank, rank-1, ..., rank-P+1 (mod P).
+// Segment j*Epr + e is (source s = rank - j, local expert e); the source
+// doubles as the rank whose ready flag the SwiGLU producer waits for and
+// the rank the down GEMM's output rows go to.  If the barrier runs out of
+// time, error 1 is recorded and every segment is left empty.
+__global__ void k_ep_meta(const int32_t* __restrict__ offsets, int P, int Epr, int rank,
+                          int64_t cap, PeerPtrs meta, const int32_t* meta_local, int32_t* flags,
+                          PeerPtrs peer_flags, int epoch, int32_t* done, int32_t* seg_start,
+                          int32_t* seg_end, int32_t* seg_expert, int32_t* seg_dst_row,
+                          int32_t* seg_src) {
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  for (int i = lane; i < P * (Epr + 1); i += 32) {
+    const int q = i / (Epr + 1), j = i % (Epr + 1);
+    const int v = j < Epr ? offsets[q * Epr + j + 1] - offsets[q * Epr + j] : offsets[q * Epr];
+    reinterpret_cast<int32_t*>(meta.p[q])[rank * (Epr + 1) + j] = v;
+  }
+  for (int e = lane; e < P * Epr; e += 32) done[e] = 0;
+  __threadfence_system();
+  __syncwarp();
+  bool ok = true;
+  if (lane < P) {
+    asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(
+                     reinterpret_cast<int32_t*>(peer_flags.p[lane]) + rank),
+                 "r"(epoch)
+                 : "memory");
+    const uint64_t t0 = globaltimer();
+    for (uint32_t it = 0;; ++it) {
+      int32_t v;
+      asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(flags + lane) : "memory");
+      if (v - epoch >= 0) break;
+      if ((it & 63u) == 63u && globaltimer() - t0 > kWaitLimitNs) {
+        ok = false;
+        break;
+      }
+      __nanosleep(64);
+    }
+  }
+  ok = __all_sync(0xffffffffu, ok);
+  if (!ok && lane == 0) atomicExch(&g_device_error, 1);
+  if (lane < P) {
+    const int s = lane;
+    const int j = (rank - s + P) % P;
+    const int32_t* m = meta_local + s * (Epr + 1);
+    int32_t run = 0;
+    for (int e = 0; e < Epr; ++e) {
+      const int q = j * Epr + e;
+      const int32_t c = ok ? m[e] : 0;
+      seg_start[q] = (int32_t)(s * cap) + run;
+      seg_end[q] = seg_start[q] + c;
+      seg_expert[q] = e;
+      seg_dst_row[q] = (ok ? m[Epr] : 0) + run;
+      seg_src[q] = s;
+      run += c;
+    }
+  }
+}
+
 }  // namespace moe
 }  // namespace rb
 
@@ -205,4 +267,88 @@ extern "C" int remora_b200_moe_ep_experts_bf16(const void* recv, const void* wg,
     return rc;
   return grouped_launch(false, h, wd, nullptr, nullptr, nullptr, rows, F, D, Epr, st,
                         seg + 2 * S, S, seg, seg + S, seg + 3 * S, seg + 4 * S, &yp);
+}
+
+// Fused path, step 1: metadata exchange + barrier + segment table + zeroed
+// completion counters (one small kernel).
+extern "C" int remora_b200_moe_ep_meta(const int32_t* offsets, int P, int E, int rank,
+                                       int64_t cap, const uint64_t* meta_ptrs,
+                                       const int32_t* meta_local, int32_t* flags,
+                                       const uint64_t* flag_ptrs, int epoch, int32_t* done,
+                                       int32_t* seg, void* stream) {
+  clear_error();
+  RB_CHECK_ARG(P >= 1 && P <= 8 && rank >= 0 && rank < P && E % P == 0 && E <= GMaxE && cap >= 0,
+               "moe_ep_meta: bad P=%d rank=%d E=%d", P, rank, E);
+  RB_CHECK_ARG(offsets && meta_local && flags && done && seg, "moe_ep_meta: null pointer");
+  RB_CHECK_ARG((int64_t)P * cap < (1ll << 31), "moe_ep_meta: P*cap exceeds 2^31 rows");
+  PeerPtrs mp, fp;
+  int rc;
+  if ((rc = peer_ptrs(meta_ptrs, P, &mp, "meta")) || (rc = peer_ptrs(flag_ptrs, P, &fp, "flag")))
+    return rc;
+  const int Epr = E / P, S = E;
+  k_ep_meta<<<1, 32, 0, as_stream(stream)>>>(offsets, P, Epr, rank, cap, mp, meta_local, flags, fp,
+                                             epoch, done, seg, seg + S, seg + 2 * S, seg + 3 * S,
+                                             seg + 4 * S);
+  RB_LAUNCH_CHECK();
+  return REMORA_B200_OK;
+}
+
+// Fused path, step 2: one cooperative kernel per rank whose extra warps
+// scatter this rank's dispatched rows into the peers' recv buffers while its
+// tcgen05 pipeline runs the SwiGLU GEMM over the received segments, each
+// segment's first tile waiting (bounded) for its source's ready flag.
+extern "C" int remora_b200_moe_ep_dispatch_swiglu_bf16(
+    const void* x, const int32_t* perm, const int32_t* offsets, int64_t n, int k, int64_t D,
+    int64_t F, int E, int P, int rank, int64_t cap, const uint64_t* recv_ptrs,
+    const uint64_t* ready_ptrs, const int32_t* ready_local, int32_t* done, int epoch,
+    const void* recv_local, const void* wg, const void* wu, void* h, const int32_t* seg,
+    void* stream) {
+  clear_error();
+  RB_CHECK_ARG(P >= 1 && P <= 8 && rank >= 0 && rank < P && E % P == 0 && E <= GMaxE,
+               "moe_ep_dispatch_swiglu: bad P=%d rank=%d E=%d", P, rank, E);
+  RB_CHECK_ARG(n >= 0 && n <= cap && k >= 1 && D > 0 && D % 8 == 0 && F > 0 && cap > 0,
+               "moe_ep_dispatch_swiglu: bad sizes");
+  RB_CHECK_ARG((int64_t)P * cap < (1ll << 31), "moe_ep_dispatch_swiglu: P*cap exceeds 2^31 rows");
+  RB_CHECK_ARG(offsets && ready_local && done && seg && recv_local &&
+                   (n == 0 || (x && perm && aligned16(x))),
+               "moe_ep_dispatch_swiglu: null or unaligned pointer");
+  PeerPtrs rp, yp;
+  int rc;
+  if ((rc = peer_ptrs(recv_ptrs, P, &rp, "recv")) || (rc = peer_ptrs(ready_ptrs, P, &yp, "ready")))
+    return rc;
+  ScatterArgs sc;
+  sc.x = static_cast<const uint16_t*>(x);
+  sc.perm = perm;
+  sc.offsets = offsets;
+  sc.n = n;
+  sc.cap = cap;
+  sc.k = k;
+  sc.D = (int)D;
+  sc.Epr = E / P;
+  sc.P = P;
+  sc.rank = rank;
+  sc.epoch = epoch;
+  sc.recv = rp;
+  sc.ready = yp;
+  sc.done = done;
+  const int S = E;
+  return grouped_launch(true, recv_local, wg, wu, h, nullptr, (int64_t)P * cap, D, F, E / P,
+                        as_stream(stream), seg + 2 * S, S, seg, seg + S, nullptr, nullptr,
+                        nullptr, seg + 4 * S, ready_local, E / P, epoch, &sc);
+}
+
+// Fused path, step 3: the down GEMM over the same segments, every output
+// row stored into its source rank's y.
+extern "C" int remora_b200_moe_ep_down_bf16(const void* h, const void* wd, const int32_t* seg,
+                                            int P, int E, int64_t cap, int64_t F, int64_t D,
+                                            const uint64_t* y_ptrs, void* stream) {
+  clear_error();
+  RB_CHECK_ARG(P >= 1 && P <= 8 && E % P == 0 && E <= GMaxE && seg, "moe_ep_down: bad arguments");
+  PeerPtrs yp;
+  int rc;
+  if ((rc = peer_ptrs(y_ptrs, P, &yp, "y"))) return rc;
+  const int S = E;
+  return grouped_launch(false, h, wd, nullptr, nullptr, nullptr, (int64_t)P * cap, F, D, E / P,
+                        as_stream(stream), seg + 2 * S, S, seg, seg + S, seg + 3 * S,
+                        seg + 4 * S, &yp);
 }

@@ -32,7 +32,7 @@ constexpr uint32_t GABytes = GBM * GBK * 2;        // 16 KB
 constexpr uint32_t GBBytes = 256 * GBK * 2;        // 32 KB: 4 boxes of [64 K x 64 N]
 constexpr uint32_t GStageBytes = GABytes + GBBytes;
 constexpr uint32_t GBarOffset = GStages * GStageBytes;
-constexpr uint32_t GEpiOffset = GBarOffset + ((256 + 6 * (GMaxE + 1) * 4 + 1023) & ~1023u);
+constexpr uint32_t GEpiOffset = GBarOffset + ((256 + 7 * (GMaxE + 1) * 4 + 1023) & ~1023u);
 constexpr uint32_t GSmemBytes = GEpiOffset + 4 * 32 * 128 + 1024;
 
 struct GroupShape {
@@ -50,6 +50,32 @@ struct GroupShape {
   const int32_t* seg_dst_row;
   const int32_t* seg_dst_rank;
   PeerPtrs dst;
+  // Optional readiness wait: before loading the first A tile of segment q
+  // the producer waits (bounded) until
+  //   wait_flags[seg_src[q] * wait_stride + seg_expert[q]] >= wait_epoch,
+  // i.e. until source rank seg_src[q] has stored every row of the segment.
+  const int32_t* seg_src;
+  const int32_t* wait_flags;
+  int wait_stride;
+  int wait_epoch;
+};
+
+// The expert-parallel dispatch carried by extra warps of the SwiGLU kernel:
+// rows p = 0 .. n-1 of this rank's dispatch order (expert-sorted, so rank q's
+// rows are [offsets[q*Epr], offsets[(q+1)*Epr])) are copied from x into
+// region `rank` of rank q's recv buffer, visiting the destinations in the
+// order rank, rank+1, ... (mod P).  When every row of global expert e is
+// stored, the last warp to finish one of them publishes `epoch` in
+// ready.p[e / Epr][rank * Epr + e % Epr].
+struct ScatterArgs {
+  const uint16_t* x;        // [T_local, D] this rank's tokens
+  const int32_t* perm;      // [n] dispatch order -> slot (token * k + j)
+  const int32_t* offsets;   // [E + 1] expert offsets of the dispatch order
+  int64_t n, cap;
+  int k, D, Epr, P, rank, epoch;
+  PeerPtrs recv;            // recv [P][cap][D] bf16 on every rank
+  PeerPtrs ready;           // ready [P * Epr] int32 on every rank
+  int32_t* done;            // [E] rows stored per expert (zero at launch)
 };
 
 struct GSmem {
@@ -88,16 +114,123 @@ __device__ __forceinline__ TileInfo group_tile(const GroupShape& s, const int* m
   return ti;
 }
 
+// Bounded acquire-wait until *f >= v (wrapping compare); false after the limit.
+__device__ __forceinline__ bool wait_flag_geq(const int32_t* f, int v) {
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    int32_t x;
+    asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(x) : "l"(f) : "memory");
+    if (x - v >= 0) return true;
+    if ((it & 63u) == 63u && globaltimer() - t0 > kWaitLimitNs) return false;
+    __nanosleep(32);
+  }
+}
+
+__device__ __forceinline__ void st_release_sys(int32_t* f, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int32_t* ep_ready_slot(const ScatterArgs& a, int e) {
+  return reinterpret_cast<int32_t*>(a.ready.p[e / a.Epr]) + a.rank * a.Epr + e % a.Epr;
+}
+
+// Scatter warps of the fused dispatch + SwiGLU kernel (see ScatterArgs).
+// Each warp copies chunks of two consecutive rows (16-byte pieces, up to 16
+// in flight per lane); chunks are spread over all scatter warps of the grid,
+// so the grid sweeps the rows in order and experts complete one after
+// another.  A warp counts the rows it stored per expert and, when it moves
+// on to another expert, fences its stores at system scope and adds the
+// count to done[e]; the add that completes done[e] publishes the flag.
+__device__ __forceinline__ void ep_scatter_warp(const ScatterArgs& a, int64_t gw, int64_t GW,
+                                                int lane) {
+  const int64_t n = a.n;
+  const int32_t* off = a.offsets;
+  const int E = a.P * a.Epr;
+  if (gw == 0) {  // experts that get no rows are complete at once
+    for (int e = lane; e < E; e += 32)
+      if (off[e + 1] == off[e]) st_release_sys(ep_ready_slot(a, e), a.epoch);
+  }
+  if (n == 0) return;
+  const int64_t base = off[a.rank * a.Epr];
+  const int D8 = a.D / 8;
+  int cur = -1, cnt = 0;
+  auto flush = [&]() {
+    if (cur < 0 || cnt == 0) return;
+    __threadfence_system();
+    __syncwarp();
+    if (lane == 0) {
+      const int total = off[cur + 1] - off[cur];
+      const int old = atomicAdd(a.done + cur, cnt);
+      if (old + cnt == total) {
+        __threadfence_system();
+        st_release_sys(ep_ready_slot(a, cur), a.epoch);
+      }
+    }
+    __syncwarp();
+  };
+  for (int64_t c = 2 * gw; c < n; c += 2 * GW) {
+    const uint4* src[2];
+    uint4* dst[2];
+    int ee[2];
+    bool ok[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      ok[u] = c + u < n;
+      int64_t p = c + u + base;
+      if (p >= n) p -= n;
+      if (!ok[u]) p = 0;
+      int lo = 0, hi = E;  // expert of p: the last e with off[e] <= p
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (off[mid] <= p) lo = mid; else hi = mid;
+      }
+      ee[u] = lo;
+      const int q = lo / a.Epr;
+      src[u] = reinterpret_cast<const uint4*>(a.x + (int64_t)(a.perm[p] / a.k) * a.D);
+      dst[u] = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.recv.p[q]) +
+                                        ((int64_t)a.rank * a.cap + (p - off[q * a.Epr])) * a.D);
+    }
+    for (int c0 = 0; c0 < D8; c0 += 8 * 32) {
+      uint4 v[2][8];
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int cc = c0 + j * 32 + lane;
+          if (ok[u] && cc < D8) v[u][j] = __ldg(src[u] + cc);
+        }
+#pragma unroll
+      for (int u = 0; u < 2; ++u)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int cc = c0 + j * 32 + lane;
+          if (ok[u] && cc < D8) dst[u][cc] = v[u][j];
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (!ok[u]) continue;
+      if (ee[u] != cur) {
+        flush();
+        cur = ee[u];
+        cnt = 0;
+      }
+      ++cnt;
+    }
+  }
+  flush();
+}
+
 __device__ __forceinline__ float silu_mul(float g, float u) {
   float e;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-g * 1.4426950408889634f));
   return (g * __frcp_rn(1.0f + e)) * u;
 }
 
-template <bool kSwiGLU>
-__global__ void __launch_bounds__(GThreads, 1)
+template <bool kSwiGLU, int kScatterWarps = 0>
+__global__ void __launch_bounds__(GThreads + 32 * kScatterWarps, 1)
     k_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
-                   const __grid_constant__ CUtensorMap tmB1, GroupShape s) {
+                   const __grid_constant__ CUtensorMap tmB1, GroupShape s, ScatterArgs sc) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -108,6 +241,7 @@ __global__ void __launch_bounds__(GThreads, 1)
   int* s_exp = s_en + (GMaxE + 1);
   int* s_drow = s_exp + (GMaxE + 1);
   int* s_drank = s_drow + (GMaxE + 1);
+  int* s_src = s_drank + (GMaxE + 1);
   // per epilogue warp: one [32 rows][128 B] staging tile, 1024-byte aligned
   uint8_t* epi_stage_base = smem + GEpiOffset;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -118,6 +252,7 @@ __global__ void __launch_bounds__(GThreads, 1)
       s_en[i] = s.seg_end[i];
       s_drow[i] = s.seg_dst_row ? s.seg_dst_row[i] : 0;
       s_drank[i] = s.seg_dst_rank ? s.seg_dst_rank[i] : 0;
+      s_src[i] = s.seg_src ? s.seg_src[i] : -1;
       const int e = s.seg_expert ? s.seg_expert[i] : i;
       s_exp[i] = (e >= 0 && e < s.E) ? e : 0;
       if (e < 0 || e >= s.E) atomicExch(&g_device_error, 2);
@@ -167,6 +302,19 @@ __global__ void __launch_bounds__(GThreads, 1)
       for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
         const TileInfo ti = group_tile(s, s_mt, s_st, s_en, s_exp, total_mt, t);
         const int n0 = ti.n * kColsPerTile;
+        if (s.wait_flags && s_src[ti.seg] >= 0) {
+          // s_src is read by this thread only: -1 marks a segment seen ready
+          const int flag = s_src[ti.seg] * s.wait_stride + s_exp[ti.seg];
+          if (!wait_flag_geq(s.wait_flags + flag, s.wait_epoch)) {
+            atomicExch(&g_device_error, 1);
+            *abort_flag = 1;
+            break;
+          }
+          // rows stored by other SMs / GPUs through the generic proxy are
+          // read below by TMA (the async proxy)
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          s_src[ti.seg] = -1;
+        }
         for (int kb = 0; kb < s.num_kb; ++kb) {
           if (!mbar_wait(&sm->empty[stage], phase ^ 1)) { *abort_flag = 1; break; }
           uint8_t* sa = smem + stage * GStageBytes;
@@ -236,6 +384,10 @@ __global__ void __launch_bounds__(GThreads, 1)
         mbar_wait(&sm->drain, 0);
       }
     }
+  } else if (warp >= 6) {
+    if (kScatterWarps > 0)
+      ep_scatter_warp(sc, (int64_t)blockIdx.x * kScatterWarps + (warp - 6),
+                      (int64_t)gridDim.x * kScatterWarps, lane);
   } else {
     const int lg = warp & 3;
     uint8_t* epi_stage = epi_stage_base + (warp - 2) * 32 * 128;

@@ -4,20 +4,27 @@ trip for split sizes).
 
 Buffers every rank can address come from torch symmetric memory, allocated
 once per ``PeerEP`` (sized for the worst case: one rank may route all of
-its T_local*k rows to one peer).  One layer on rank r:
+its T_local*k rows to one peer).  One layer on rank r (``fused=True``, the
+default):
 
   router + top-k, dispatch over all E experts              (kernels)
-  scatter: row p -> region r of rank (expert // Epr)'s recv (kernel, NVLink)
-  barrier                                                   (kernel, bounded)
-  segments from meta; SwiGLU grouped GEMM; down grouped GEMM whose epilogue
-  stores each output row into its source rank's y           (kernels, NVLink)
+  meta: counts -> every peer, barrier, segment table        (kernel, bounded)
+  dispatch + SwiGLU: one cooperative kernel; its scatter warps copy row p
+  into region r of rank (expert // Epr)'s recv and raise that rank's ready
+  flag when its rows are stored, while its tcgen05 pipeline computes the
+  SwiGLU GEMM over the received segments, sources in arrival order, each
+  waiting (bounded) for its source's flag                   (kernel, NVLink)
+  down grouped GEMM whose epilogue stores each output row
+  into its source rank's y                                  (kernel, NVLink)
   barrier                                                   (kernel, bounded)
   combine of y in slot order                                (kernel)
 
-The two barriers also order consecutive layers: a rank writes a peer's
-recv / meta / y only after every rank has finished reading them.  Results
-are bit-identical to the single-GPU layer (each row's expert output depends
-only on that row and its expert's weights).
+``fused=False`` runs the exchange and the GEMMs one after the other
+(scatter, barrier, segments, SwiGLU GEMM, down GEMM).  The barriers also
+order consecutive layers: a rank writes a peer's recv / meta / y only after
+every rank has finished reading them.  Results are bit-identical to the
+single-GPU layer (each row's expert output depends only on that row and its
+expert's weights).
 """
 from __future__ import annotations
 
@@ -32,7 +39,8 @@ def _align(n: int, a: int = 256) -> int:
 
 
 class PeerEP:
-    def __init__(self, T_local: int, D: int, F: int, E: int, k: int, group=None, device=None):
+    def __init__(self, T_local: int, D: int, F: int, E: int, k: int, group=None, device=None,
+                 fused: bool = True):
         import torch.distributed._symmetric_memory as symm_mem
 
         import remora_b200 as rb
@@ -48,8 +56,10 @@ class PeerEP:
         self.cap = T_local * k
         self.device = device or torch.device("cuda", torch.cuda.current_device())
         P, cap = self.P, self.cap
+        self.fused = fused
         self.off_flags = 0
-        self.off_meta = _align(P * 4)
+        self.off_ready = _align(P * 4)
+        self.off_meta = self.off_ready + _align(E * 4)
         self.off_recv = self.off_meta + _align(P * (self.Epr + 1) * 4)
         self.off_y = self.off_recv + _align(P * cap * D * 2)
         total = self.off_y + _align(cap * D * 2)
@@ -66,15 +76,19 @@ class PeerEP:
         base = list(self.hdl.buffer_ptrs)
         arr = lambda off: (ctypes.c_uint64 * P)(*[b + off for b in base])
         self.flag_ptrs, self.meta_ptrs = arr(self.off_flags), arr(self.off_meta)
+        self.ready_ptrs = arr(self.off_ready)
         self.recv_ptrs, self.y_ptrs = arr(self.off_recv), arr(self.off_y)
         view = lambda off, n, dt: self.buf[off:off + n * torch.tensor([], dtype=dt).element_size()].view(dt)
         self.flags = view(self.off_flags, P, torch.int32)
+        self.ready = view(self.off_ready, E, torch.int32)
+        self.done = torch.zeros(E, dtype=torch.int32, device=self.device)
         self.meta = view(self.off_meta, P * (self.Epr + 1), torch.int32)
         self.recv = view(self.off_recv, P * cap * D, torch.bfloat16).view(P * cap, D)
         self.y = view(self.off_y, cap * D, torch.bfloat16).view(cap, D)
         self.h = torch.empty(P * cap, F, dtype=torch.bfloat16, device=self.device)
         self.seg = torch.empty(5 * P * self.Epr, dtype=torch.int32, device=self.device)
         self.epoch = 0
+        self.layer = 0
         self.profile = False   # when True, forward() records per-phase CUDA events
         self.phase_ms = {}
         dist.barrier(group)
@@ -84,9 +98,10 @@ class PeerEP:
         self.rb._check(self.rb.lib().remora_b200_moe_ep_barrier(
             self.flags.data_ptr(), self.flag_ptrs, self.P, self.rank, self.epoch, stream))
 
-    def forward(self, x, wr, wg_local, wu_local, wd_local):
+    def forward(self, x, wr, wg_local, wu_local, wd_local, out=None):
         """x [T_local, D]; wr [D, E]; this rank's experts wg/wu [Epr, D, F],
-        wd [Epr, F, D].  Returns out [T_local, D] bf16."""
+        wd [Epr, F, D].  Returns out [T_local, D] bf16 (written into `out`
+        when given)."""
         rb, L = self.rb, self.rb.lib()
         if x.shape != (self.T, self.D) or wg_local.shape[0] != self.Epr:
             raise ValueError("shapes differ from the ones this PeerEP was built for")
@@ -104,6 +119,9 @@ class PeerEP:
         idx, w = rb.moe_router_topk(x, wr, self.k)
         counts, offsets, perm, inv = rb.moe_dispatch(idx, self.E)
         mark("route+dispatch")
+        if self.fused:
+            return self._forward_fused(x, w, offsets, perm, inv, wg_local, wu_local, wd_local,
+                                       cs, mark, marks, out)
         rb._check(L.remora_b200_moe_ep_scatter_bf16(
             x.data_ptr(), perm.data_ptr(), offsets.data_ptr(), self.cap, self.k, self.D, self.E,
             self.P, self.rank, self.cap, self.recv_ptrs, self.meta_ptrs, stream))
@@ -120,7 +138,38 @@ class PeerEP:
         mark("experts")
         self._barrier(stream)
         mark("barrier2")
-        out = rb.moe_combine(self.y, inv, w)
+        out = rb.moe_combine(self.y, inv, w, out=out)
+        mark("combine")
+        if self.profile:
+            marks[-1][1].synchronize()
+            self.phase_ms = {b[0]: a[1].elapsed_time(b[1]) for a, b in zip(marks, marks[1:])}
+        return out
+
+    def _forward_fused(self, x, w, offsets, perm, inv, wg_local, wu_local, wd_local, cs, mark,
+                       marks, out):
+        rb, L = self.rb, self.rb.lib()
+        stream = cs.cuda_stream
+        self.epoch += 1
+        rb._check(L.remora_b200_moe_ep_meta(
+            offsets.data_ptr(), self.P, self.E, self.rank, self.cap, self.meta_ptrs,
+            self.meta.data_ptr(), self.flags.data_ptr(), self.flag_ptrs, self.epoch,
+            self.done.data_ptr(), self.seg.data_ptr(), stream))
+        mark("meta")
+        self.layer += 1
+        rb._check(L.remora_b200_moe_ep_dispatch_swiglu_bf16(
+            x.data_ptr(), perm.data_ptr(), offsets.data_ptr(), self.cap, self.k, self.D, self.F,
+            self.E, self.P, self.rank, self.cap, self.recv_ptrs, self.ready_ptrs,
+            self.ready.data_ptr(), self.done.data_ptr(), self.layer, self.recv.data_ptr(),
+            wg_local.contiguous().data_ptr(), wu_local.contiguous().data_ptr(),
+            self.h.data_ptr(), self.seg.data_ptr(), stream))
+        mark("dispatch+swiglu")
+        rb._check(L.remora_b200_moe_ep_down_bf16(
+            self.h.data_ptr(), wd_local.contiguous().data_ptr(), self.seg.data_ptr(), self.P,
+            self.E, self.cap, self.F, self.D, self.y_ptrs, stream))
+        mark("down")
+        self._barrier(stream)
+        mark("barrier2")
+        out = rb.moe_combine(self.y, inv, w, out=out)
         mark("combine")
         if self.profile:
             marks[-1][1].synchronize()

@@ -1,6 +1,10 @@
-"""Expert-parallel MoE over NCCL on 2+ GPUs: the EP layer must equal the
-single-GPU layer bit for bit (each row's expert output depends only on the
-row and its expert).  Skipped when fewer than 2 GPUs are visible."""
+"""Expert-parallel MoE on 2+ GPUs (NCCL all-to-all, and the peer-memory
+paths with the scatter fused into the SwiGLU GEMM or run as its own
+kernel): the EP layer must equal the single-GPU layer bit for bit (each
+row's expert output depends only on the row and its expert).  The
+peer-memory paths run three consecutive layers on two different inputs,
+so rows left over from the previous layer cannot pass for this layer's.
+Skipped when fewer than 2 GPUs are visible."""
 import datetime
 import os
 import socket
@@ -45,28 +49,34 @@ def _worker(rank, world, port, cfg, outdir, mode="nccl"):
     for t, s, sig in ((x, 30, 1.0), (wr, 31, 0.02), (wg, 32, 0.02), (wu, 33, 0.02),
                       (wd, 34, 0.02)):
         rb.fill_normal(t, rb.stream_key(s), 0.0, sig)
+    x2 = torch.empty_like(x)
+    rb.fill_normal(x2, rb.stream_key(35), 0.0, 1.0)
     tl, Epr = T // world, E // world
-    xl = x[rank * tl:(rank + 1) * tl].contiguous()
+    sl = slice(rank * tl, (rank + 1) * tl)
+    xl, x2l = x[sl].contiguous(), x2[sl].contiguous()
     wl = [w_[rank * Epr:(rank + 1) * Epr].contiguous() for w_ in (wg, wu, wd)]
-    ref = rb.moe_layer(x, wr, wg, wu, wd, k)[rank * tl:(rank + 1) * tl]
+    ref = rb.moe_layer(x, wr, wg, wu, wd, k)[sl]
+    ref2 = rb.moe_layer(x2, wr, wg, wu, wd, k)[sl]
     same = True
     if mode == "nccl":
         outs = [moe_ep_forward(xl, wr, *wl, k, E)]
+        refs = [ref]
     else:
         from remora_b200.ep_p2p import PeerEP
 
-        ep = PeerEP(tl, D, F, E, k)
-        outs = [ep.forward(xl, wr, *wl).clone() for _ in range(3)]  # consecutive layers
+        ep = PeerEP(tl, D, F, E, k, fused=mode == "p2p")
+        outs = [ep.forward(xi, wr, *wl).clone() for xi in (xl, x2l, xl)]  # consecutive layers
+        refs = [ref, ref2, ref]
     rb.synchronize_and_check(dev)
-    for out in outs:
-        same = same and torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    for out, r in zip(outs, refs):
+        same = same and torch.equal(out.view(torch.int16), r.view(torch.int16))
     with open(os.path.join(outdir, f"r{rank}.txt"), "w") as f:
         f.write("same" if same else "differ")
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["nccl", "p2p"])
+@pytest.mark.parametrize("mode", ["nccl", "p2p", "p2p-split"])
 @pytest.mark.parametrize("cfg", [(4096, 512, 256, 16, 4), (8192, 2048, 1536, 64, 8)])
 def test_ep_matches_single_gpu_layer(rb, tmp_path, cfg, mode):
     world = min(torch.cuda.device_count(), 8)
