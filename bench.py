@@ -96,11 +96,14 @@ class ClockSampler:
                 pass
             self._stop.wait(self.period)
 
-    def __enter__(self):
-        if self.ok:
+    def start(self):
+        if self.ok and self._thread is None:
             self._thread = threading.Thread(target=self._run, daemon=True)
             self._thread.start()
         return self
+
+    def __enter__(self):
+        return self.start()
 
     def __exit__(self, *a):
         if self._thread:
@@ -282,11 +285,12 @@ def bench_gemm(args, world, rank, local):
 
     for _ in range(args.warmup):
         step()
+    clk = ClockSampler(local).start()  # NVML set-up before the barrier that aligns the ranks
     torch.cuda.synchronize(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with clk:
         ev0.record(stream)
         for _ in range(args.steps):
             step()
@@ -398,11 +402,12 @@ def bench_moe(args, world, rank, local):
 
     for _ in range(args.warmup):
         step()
+    clk = ClockSampler(local).start()  # NVML set-up before the barrier that aligns the ranks
     rb.synchronize_and_check(dev)
     barrier(world)
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with clk:
         ev0.record(stream)
         for _ in range(args.steps):
             step()
@@ -516,12 +521,13 @@ def bench_moe_ep(args, world, rank, local):
 
     for _ in range(args.warmup):
         step()
+    clk = ClockSampler(local).start()  # NVML set-up before the barrier that aligns the ranks
     rb.synchronize_and_check(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with clk:
         ev0.record(stream)
         for _ in range(args.steps):
             step()
@@ -602,11 +608,12 @@ def bench_attention(args, world, rank, local):
 
     for _ in range(args.warmup):
         step()
+    clk = ClockSampler(local).start()  # NVML set-up before the barrier that aligns the ranks
     torch.cuda.synchronize(dev)
     barrier(world)
     stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with clk:
         ev0.record(stream)
         for _ in range(args.steps):
             step()
@@ -669,10 +676,11 @@ def bench_elementwise(args, world, rank, local):
     stream = torch.cuda.current_stream(dev)
     for _ in range(args.warmup):
         rb.scale_add_exp(s, b, 0.125, out=o)
+    clk = ClockSampler(local).start()  # NVML set-up before the barrier that aligns the ranks
     torch.cuda.synchronize(dev)
     barrier(world)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    with clk:
         ev0.record(stream)
         for _ in range(args.steps):
             rb.scale_add_exp(s, b, 0.125, out=o)

@@ -138,9 +138,15 @@ __device__ __forceinline__ int32_t* ep_ready_slot(const ScatterArgs& a, int e) {
 // Each warp copies chunks of two consecutive rows (16-byte pieces, up to 16
 // in flight per lane); chunks are spread over all scatter warps of the grid,
 // so the grid sweeps the rows in order and experts complete one after
-// another.  A warp counts the rows it stored per expert and, when it moves
-// on to another expert, fences its stores at system scope and adds the
-// count to done[e]; the add that completes done[e] publishes the flag.
+// another.  A warp counts the rows it stored per expert and keeps the
+// (expert, count) pairs it has finished in a pending list, one entry per
+// lane.  When kPending experts are pending (and at the end) it fences its
+// stores at system scope once and each pending lane adds its count to
+// done[e]; the add that completes done[e] publishes the flag.  One fence
+// per kPending experts keeps the warp from waiting on NVLink
+// acknowledgements after every chunk.
+constexpr int kPending = 4;
+
 __device__ __forceinline__ void ep_scatter_warp(const ScatterArgs& a, int64_t gw, int64_t GW,
                                                 int lane) {
   const int64_t n = a.n;
@@ -153,20 +159,31 @@ __device__ __forceinline__ void ep_scatter_warp(const ScatterArgs& a, int64_t gw
   if (n == 0) return;
   const int64_t base = off[a.rank * a.Epr];
   const int D8 = a.D / 8;
-  int cur = -1, cnt = 0;
+  int cur = -1, cnt = 0;         // expert being copied, rows of it stored so far
+  int pend_e = -1, pend_c = 0;    // this lane's entry of the pending list
+  int npend = 0;                  // warp-uniform length of the pending list
   auto flush = [&]() {
-    if (cur < 0 || cnt == 0) return;
+    if (npend == 0) return;
     __threadfence_system();
     __syncwarp();
-    if (lane == 0) {
-      const int total = off[cur + 1] - off[cur];
-      const int old = atomicAdd(a.done + cur, cnt);
-      if (old + cnt == total) {
+    if (lane < npend) {
+      const int total = off[pend_e + 1] - off[pend_e];
+      const int old = atomicAdd(a.done + pend_e, pend_c);
+      if (old + pend_c == total) {
         __threadfence_system();
-        st_release_sys(ep_ready_slot(a, cur), a.epoch);
+        st_release_sys(ep_ready_slot(a, pend_e), a.epoch);
       }
     }
     __syncwarp();
+    npend = 0;
+  };
+  auto retire = [&]() {  // move (cur, cnt) to the pending list
+    if (cur < 0 || cnt == 0) return;
+    if (lane == npend) {
+      pend_e = cur;
+      pend_c = cnt;
+    }
+    if (++npend == kPending) flush();
   };
   for (int64_t c = 2 * gw; c < n; c += 2 * GW) {
     const uint4* src[2];
@@ -211,13 +228,14 @@ __device__ __forceinline__ void ep_scatter_warp(const ScatterArgs& a, int64_t gw
     for (int u = 0; u < 2; ++u) {
       if (!ok[u]) continue;
       if (ee[u] != cur) {
-        flush();
+        retire();
         cur = ee[u];
         cnt = 0;
       }
       ++cnt;
     }
   }
+  retire();
   flush();
 }
 
