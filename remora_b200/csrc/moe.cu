@@ -21,7 +21,8 @@ namespace moe {
 // top-k indices are bit-identical to it.  A bf16 x bf16 product is exact in
 // fp32, so fmaf(a, b, acc) == acc + a*b here.
 constexpr int kRouterThreads = 256;
-constexpr int kRouterDC = 64;           // d per shared-memory chunk
+constexpr int kRouterDCh = 32;             // d per shared-memory chunk
+constexpr int kRowPadF = kRouterDCh + 4;   // padded f32 row (16-byte aligned rows)
 
 __device__ __forceinline__ bool topk_before(float a, int ia, float b, int ib) {
   const bool an = a != a, bn = b != b;
@@ -30,68 +31,97 @@ __device__ __forceinline__ bool topk_before(float a, int ia, float b, int ib) {
   return ia < ib;
 }
 
-// Register-blocked router.  Thread (token group tg, expert group eg) owns an
-// RT x 8 block of (token, expert) accumulators: tokens tg*RT .. +RT-1 of the
-// block, experts eg*8 .. eg*8+7.  Each accumulator is still one serial fp32
-// chain over d in increasing order (bit-exact), but a 4-d step costs RT + 8
-// shared loads for 32*RT FMAs.  Tokens and router chunks are converted to f32
-// once while staging.  NG = expert groups per token, a power of two <= 32:
-// the NG lanes of a token are adjacent, so top-k is a segmented shuffle.
-constexpr int kRouterDCh = 32;             // d per chunk
-constexpr int kRowPadF = kRouterDCh + 4;   // padded f32 row (conflict-free 16-byte loads)
-
-template <int RT, int NG>
-__global__ void __launch_bounds__(kRouterThreads, 1)
+// Router, expert-lane form.  A warp is LT = 32/LE token groups of LE lanes
+// (LE a power of two, 1..32, chosen by the host).  Lane (tg, le) owns RT
+// tokens of its group and the experts le, le+LE, ..., le+(EPL-1)*LE, one
+// accumulator each.  Every accumulator is one serial fp32 chain over d in
+// increasing order (bit-exact).  Per 4-d step a lane loads EPL rows of the
+// staged router chunk (one row per expert, the same row for all token
+// groups of a warp) and RT token rows (one address per token group: the LE
+// lanes of a group read it as a broadcast), then issues 4*RT*EPL FMAs, so
+// the shared-memory traffic per FMA falls as RT and EPL grow.  Tokens and
+// router chunks are converted to f32 once while staging; the next chunk's
+// global loads are issued into registers before the current chunk is used.
+// Top-k: per token, a segmented butterfly over the LE lanes of its group.
+// Host contract: RT <= LE (at most 256 tokens per block), E % 8 == 0 or
+// E <= 128, k <= 16.
+template <int RT, int EPL>
+__global__ void __launch_bounds__(kRouterThreads)
     k_router_topk(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr, int T, int D,
-                  int E, int k, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
+                  int E, int k, int LE, int32_t* __restrict__ idx_out,
+                  float* __restrict__ w_out) {
   extern __shared__ __align__(16) uint8_t sm_raw[];
-  constexpr int TG = kRouterThreads / NG;  // token groups per block
-  constexpr int TPB = TG * RT;             // tokens per block
-  constexpr int EP = NG * 8;               // padded expert count
+  constexpr int kWarps = kRouterThreads / 32;
+  constexpr int kDC8 = kRouterDCh / 8;
+  const int LT = 32 / LE;              // token groups per warp
+  const int TGB = kWarps * LT;         // token groups per block
+  const int TPB = TGB * RT;            // tokens per block
+  const int EP = LE * EPL;             // staged router rows (>= E)
   float* xs = reinterpret_cast<float*>(sm_raw);  // [TPB][kRowPadF]
-  float* ws = xs + TPB * kRowPadF;               // [EP][kRowPadF] (transposed chunk)
-  const int tid = threadIdx.x;
-  const int eg = tid % NG, tg = tid / NG;
+  float* ws = xs + TPB * kRowPadF;               // [EP][kRowPadF] (router chunk, transposed)
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tg = lane / LE, le = lane % LE;
+  const int gtg = warp * LT + tg;      // token group within the block
   const int t0 = blockIdx.x * TPB;
-  float acc[RT][8];
+  float acc[RT][EPL];
 #pragma unroll
   for (int r = 0; r < RT; ++r)
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[r][i] = 0.0f;
+    for (int j = 0; j < EPL; ++j) acc[r][j] = 0.0f;
+  // rows beyond E stay zero (their experts are never selected)
+  for (int i = tid; i < (EP - E) * kRowPadF; i += kRouterThreads) ws[E * kRowPadF + i] = 0.0f;
 
-  // The next chunk's global loads are issued into registers before the
-  // current chunk is computed, so their latency overlaps the FMAs.
-  constexpr int XPT = (TPB * (kRouterDCh / 8) + kRouterThreads - 1) / kRouterThreads;
-  constexpr int WPT = (kRouterDCh * EP + kRouterThreads - 1) / kRouterThreads;
-  uint4 xpre[XPT];
-  uint16_t wpre[WPT];
+  // Block token q = g*RT + r (token group g) lives in smem row r*TGB + g: the
+  // LT token groups of a warp read LT adjacent rows for a given r.
+  // Router chunk: with E % 8 == 0 each thread moves 8 experts x 1 d (one
+  // 16-byte load; the lanes of a warp take consecutive d, so the transposed
+  // shared stores are conflict-free); otherwise single values.
+  const bool vec_w = (E % 8) == 0;
+  const int nx = TPB * kDC8;                              // x pieces of 8 per chunk
+  const int nw = vec_w ? kRouterDCh * (E / 8) : kRouterDCh * E;
+  constexpr int kXPT = 256 * kDC8 / kRouterThreads;       // TPB <= 256
+  constexpr int kWPT = 4;                                 // 16-byte pieces (E <= 256)
+  constexpr int kWPS = 16;                                // single values (E <= 128)
+  uint4 xpre[kXPT];
+  uint32_t wreg[4 * kWPT];
   auto load_chunk = [&](int d0) {
     const int dc = min(kRouterDCh, D - d0);
 #pragma unroll
-    for (int j = 0; j < XPT; ++j) {
+    for (int j = 0; j < kXPT; ++j) {
       const int i = tid + j * kRouterThreads;
-      const int row = i / (kRouterDCh / 8), c8 = (i % (kRouterDCh / 8)) * 8;
+      const int row = i / kDC8, c8 = (i % kDC8) * 8;
       xpre[j] = make_uint4(0, 0, 0, 0);
-      if (i < TPB * (kRouterDCh / 8) && t0 + row < T && c8 < dc)
+      if (i < nx && t0 + row < T && c8 < dc)
         xpre[j] = *reinterpret_cast<const uint4*>(x + (int64_t)(t0 + row) * D + d0 + c8);
     }
+    if (vec_w) {
 #pragma unroll
-    for (int j = 0; j < WPT; ++j) {
-      const int i = tid + j * kRouterThreads;
-      const int dd = i / EP, ee = i % EP;
-      wpre[j] = (i < kRouterDCh * EP && dd < dc && ee < E) ? wr[(int64_t)(d0 + dd) * E + ee]
-                                                             : (uint16_t)0;
+      for (int j = 0; j < kWPT; ++j) {
+        const int i = tid + j * kRouterThreads;
+        const int dd = i % kRouterDCh, e0 = (i / kRouterDCh) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (i < nw && dd < dc) v = *reinterpret_cast<const uint4*>(wr + (int64_t)(d0 + dd) * E + e0);
+        wreg[4 * j] = v.x;
+        wreg[4 * j + 1] = v.y;
+        wreg[4 * j + 2] = v.z;
+        wreg[4 * j + 3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kWPS; ++j) {
+        const int i = tid + j * kRouterThreads;
+        const int dd = i % kRouterDCh, e = i / kRouterDCh;
+        wreg[j] = (i < nw && dd < dc) ? wr[(int64_t)(d0 + dd) * E + e] : 0u;
+      }
     }
   };
   auto store_chunk = [&]() {
 #pragma unroll
-    for (int j = 0; j < XPT; ++j) {
+    for (int j = 0; j < kXPT; ++j) {
       const int i = tid + j * kRouterThreads;
-      if (i >= TPB * (kRouterDCh / 8)) break;
-      const int row = i / (kRouterDCh / 8), c8 = (i % (kRouterDCh / 8)) * 8;
-      // token q = tg*RT + r lives in smem row r*TG + tg: the token groups of a
-      // warp then read adjacent rows (conflict-free 16-byte loads)
-      const int srow = (row % RT) * TG + row / RT;
+      if (i >= nx) break;
+      const int row = i / kDC8, c8 = (i % kDC8) * 8;
+      const int srow = (row % RT) * TGB + row / RT;
       const uint4 v = xpre[j];
       float4* dst = reinterpret_cast<float4*>(xs + srow * kRowPadF + c8);
       dst[0] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u),
@@ -99,16 +129,30 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
       dst[1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xffff0000u),
                            __uint_as_float(v.w << 16), __uint_as_float(v.w & 0xffff0000u));
     }
+    if (vec_w) {
 #pragma unroll
-    for (int j = 0; j < WPT; ++j) {
-      const int i = tid + j * kRouterThreads;
-      if (i >= kRouterDCh * EP) break;
-      const int dd = i / EP, ee = i % EP;
-      // expert ee = eg*8 + q lives in row q*NG + eg (adjacent rows across eg)
-      ws[((ee & 7) * NG + (ee >> 3)) * kRowPadF + dd] = __uint_as_float((uint32_t)wpre[j] << 16);
+      for (int j = 0; j < kWPT; ++j) {
+        const int i = tid + j * kRouterThreads;
+        if (i >= nw) break;
+        float* col = ws + (i / kRouterDCh) * 8 * kRowPadF + i % kRouterDCh;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          col[(2 * q) * kRowPadF] = __uint_as_float(wreg[4 * j + q] << 16);
+          col[(2 * q + 1) * kRowPadF] = __uint_as_float(wreg[4 * j + q] & 0xffff0000u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < kWPS; ++j) {
+        const int i = tid + j * kRouterThreads;
+        if (i >= nw) break;
+        ws[(i / kRouterDCh) * kRowPadF + i % kRouterDCh] = __uint_as_float(wreg[j] << 16);
+      }
     }
   };
 
+  const float* wrow = ws + le * kRowPadF;
+  const float* xrow = xs + gtg * kRowPadF;
   load_chunk(0);
   for (int d0 = 0; d0 < D; d0 += kRouterDCh) {
     store_chunk();
@@ -116,61 +160,58 @@ __global__ void __launch_bounds__(kRouterThreads, 1)
     if (d0 + kRouterDCh < D) load_chunk(d0 + kRouterDCh);
 #pragma unroll 2
     for (int dd = 0; dd < kRouterDCh; dd += 4) {
-      float4 wv[8];
+      float4 wv[EPL];
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        wv[i] = *reinterpret_cast<const float4*>(ws + (i * NG + eg) * kRowPadF + dd);
+      for (int j = 0; j < EPL; ++j)
+        wv[j] = *reinterpret_cast<const float4*>(wrow + j * LE * kRowPadF + dd);
 #pragma unroll
       for (int r = 0; r < RT; ++r) {
-        const float4 xv = *reinterpret_cast<const float4*>(xs + (r * TG + tg) * kRowPadF + dd);
+        const float4 xv = *reinterpret_cast<const float4*>(xrow + r * TGB * kRowPadF + dd);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          acc[r][i] = fmaf(xv.x, wv[i].x, acc[r][i]);
-          acc[r][i] = fmaf(xv.y, wv[i].y, acc[r][i]);
-          acc[r][i] = fmaf(xv.z, wv[i].z, acc[r][i]);
-          acc[r][i] = fmaf(xv.w, wv[i].w, acc[r][i]);
+        for (int j = 0; j < EPL; ++j) {
+          acc[r][j] = fmaf(xv.x, wv[j].x, acc[r][j]);
+          acc[r][j] = fmaf(xv.y, wv[j].y, acc[r][j]);
+          acc[r][j] = fmaf(xv.z, wv[j].z, acc[r][j]);
+          acc[r][j] = fmaf(xv.w, wv[j].w, acc[r][j]);
         }
       }
     }
     __syncthreads();
   }
 
-  // top-k per token over the NG lanes of its group (8 candidates per lane)
-  const int lane = tid & 31;
-  const unsigned gmask = (NG == 32) ? 0xffffffffu : (((1u << NG) - 1u) << (lane & ~(NG - 1)));
+  // top-k per token over the LE lanes of its group (EPL candidates per lane)
 #pragma unroll
-  for (int r = 0; r < RT; ++r) {  // unrolled: acc[r][i] stays in registers
-    const int t = t0 + tg * RT + r;
+  for (int r = 0; r < RT; ++r) {  // unrolled: acc[r][j] stays in registers
+    const int t = t0 + gtg * RT + r;
     uint32_t used = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (eg * 8 + i >= E) used |= 1u << i;
+    for (int j = 0; j < EPL; ++j)
+      if (le + j * LE >= E) used |= 1u << j;
     float sel_v[16];
     int sel_i[16];
-    for (int j = 0; j < k; ++j) {
+    for (int s = 0; s < k; ++s) {
       float bv = 0.0f;
       int bi = 0x7fffffff;
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (!(used >> i & 1u) &&
-            (bi == 0x7fffffff || topk_before(acc[r][i], eg * 8 + i, bv, bi))) {
-          bv = acc[r][i];
-          bi = eg * 8 + i;
+      for (int j = 0; j < EPL; ++j)
+        if (!(used >> j & 1u) &&
+            (bi == 0x7fffffff || topk_before(acc[r][j], le + j * LE, bv, bi))) {
+          bv = acc[r][j];
+          bi = le + j * LE;
         }
-#pragma unroll
-      for (int off = NG / 2; off > 0; off >>= 1) {
-        const float ov = __shfl_xor_sync(gmask, bv, off, NG);
-        const int oi = __shfl_xor_sync(gmask, bi, off, NG);
+      for (int off = LE / 2; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off, LE);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off, LE);
         if (oi != 0x7fffffff && (bi == 0x7fffffff || topk_before(ov, oi, bv, bi))) {
           bv = ov;
           bi = oi;
         }
       }
-      sel_v[j] = bv;
-      sel_i[j] = bi;
-      if (bi >> 3 == eg) used |= 1u << (bi & 7);
+      sel_v[s] = bv;
+      sel_i[s] = bi;
+      if (bi % LE == le) used |= 1u << (bi / LE);
     }
-    if (eg == 0 && t < T) {
+    if (le == 0 && t < T) {
       // stablehlo.reduce maximum (init -inf), exp, reduce add (init 0), divide
       float m = -INFINITY;
       for (int j = 0; j < k; ++j) m = (sel_v[j] != sel_v[j] || sel_v[j] > m) ? sel_v[j] : m;

@@ -19,41 +19,66 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
   RB_CHECK_ARG(x && wr && idx && w, "router: null pointer");
   RB_CHECK_ARG(aligned16(x), "router: x must be 16-byte aligned");
   RB_CHECK_ARG(T < (1ll << 31) && D < (1ll << 31), "router: sizes exceed 2^31");
-  // expert groups of 8 per token (power of two) and tokens per thread: as
-  // many as keep at least two blocks per SM (small T gets more blocks)
-  int ng = 1;
-  while (ng * 8 < E) ng *= 2;
-  int rt = ng >= 8 ? 4 : (ng >= 2 ? 2 : 1);
-  while (rt > 1 && (T + (kRouterThreads / ng) * rt - 1) / ((kRouterThreads / ng) * rt) <
-                       2 * (int64_t)num_sms())
-    rt /= 2;
-  const int tpb = (kRouterThreads / ng) * rt;
-  const size_t smem = ((size_t)tpb + (size_t)ng * 8) * kRowPadF * 4;
+  RB_CHECK_ARG(E % 8 == 0 || E <= 128, "router: E=%d must be a multiple of 8 above 128", E);
+  // Lanes per token group LE (a power of two) and experts per lane EPL with
+  // LE * EPL >= E; tokens per lane RT as large as still leaves at least 3/4
+  // of the SMs a block (RT <= LE, RT * EPL <= 32 accumulators).  The shared
+  // memory delivers 16 (RT + EPL) bytes per 4 RT EPL FMAs, so larger blocks
+  // of (tokens x experts) per lane are faster until the grid runs short.
+  // Measured on B200 (T, D, E): (8192, 2048, 64) 138 us with LE 16, EPL 4,
+  // RT 4; (65536, 2048, 64) 689 us with RT 8; (8192, 4096, 8) 99 us with LE 8,
+  // EPL 1, RT 2.
+  int epl = 1, le = 1;
+  if (E > 128) {
+    epl = 8;
+    le = 32;
+  } else if (E > 64) {
+    epl = 4;
+    le = 32;
+  } else if (E > 32) {
+    epl = 4;
+    le = 16;
+  } else {
+    while (le < E) le *= 2;
+  }
+  auto tokens_per_block = [&](int rt) { return (int64_t)(kRouterThreads / 32) * (32 / le) * rt; };
+  int rt = 1;
+  for (int c = 16; c > 1; c /= 2)
+    if (c <= le && c * epl <= 32 &&
+        4 * ((T + tokens_per_block(c) - 1) / tokens_per_block(c)) >= 3 * (int64_t)num_sms()) {
+      rt = c;
+      break;
+    }
+  const int64_t tpb = tokens_per_block(rt);
+  const size_t smem = (size_t)(tpb + le * epl) * kRowPadF * 4;
   const int64_t grid = (T + tpb - 1) / tpb;
   auto launch = [&](auto kern) -> int {
     if (smem > 48 * 1024)
       RB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     kern<<<(unsigned)grid, kRouterThreads, smem, st>>>(static_cast<const uint16_t*>(x),
                                                        static_cast<const uint16_t*>(wr), (int)T,
-                                                       (int)D, E, k, idx, w);
+                                                       (int)D, E, k, le, idx, w);
     return REMORA_B200_OK;
   };
   int rc;
-  switch (ng * 8 + rt) {
-    case 1 * 8 + 1: rc = launch(k_router_topk<1, 1>); break;
-    case 2 * 8 + 1: rc = launch(k_router_topk<1, 2>); break;
-    case 2 * 8 + 2: rc = launch(k_router_topk<2, 2>); break;
-    case 4 * 8 + 1: rc = launch(k_router_topk<1, 4>); break;
-    case 4 * 8 + 2: rc = launch(k_router_topk<2, 4>); break;
-    case 8 * 8 + 1: rc = launch(k_router_topk<1, 8>); break;
-    case 8 * 8 + 2: rc = launch(k_router_topk<2, 8>); break;
-    case 8 * 8 + 4: rc = launch(k_router_topk<4, 8>); break;
-    case 16 * 8 + 1: rc = launch(k_router_topk<1, 16>); break;
-    case 16 * 8 + 2: rc = launch(k_router_topk<2, 16>); break;
-    case 16 * 8 + 4: rc = launch(k_router_topk<4, 16>); break;
-    case 32 * 8 + 1: rc = launch(k_router_topk<1, 32>); break;
-    case 32 * 8 + 2: rc = launch(k_router_topk<2, 32>); break;
-    default: rc = launch(k_router_topk<4, 32>); break;
+  switch (epl * 100 + rt) {
+    case 101: rc = launch(k_router_topk<1, 1>); break;
+    case 102: rc = launch(k_router_topk<2, 1>); break;
+    case 104: rc = launch(k_router_topk<4, 1>); break;
+    case 108: rc = launch(k_router_topk<8, 1>); break;
+    case 116: rc = launch(k_router_topk<16, 1>); break;
+    case 201: rc = launch(k_router_topk<1, 2>); break;
+    case 202: rc = launch(k_router_topk<2, 2>); break;
+    case 204: rc = launch(k_router_topk<4, 2>); break;
+    case 208: rc = launch(k_router_topk<8, 2>); break;
+    case 216: rc = launch(k_router_topk<16, 2>); break;
+    case 401: rc = launch(k_router_topk<1, 4>); break;
+    case 402: rc = launch(k_router_topk<2, 4>); break;
+    case 404: rc = launch(k_router_topk<4, 4>); break;
+    case 408: rc = launch(k_router_topk<8, 4>); break;
+    case 801: rc = launch(k_router_topk<1, 8>); break;
+    case 802: rc = launch(k_router_topk<2, 8>); break;
+    default: rc = launch(k_router_topk<4, 8>); break;
   }
   if (rc) return rc;
   RB_LAUNCH_CHECK();

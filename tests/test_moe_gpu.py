@@ -22,7 +22,9 @@ def _moe_inputs(orc, T, D, F, E, seed=42):
 
 
 @pytest.mark.parametrize("T,D,E,k", [(1000, 256, 8, 2), (333, 512, 64, 8), (77, 64, 6, 3),
-                                     (4096, 1024, 16, 4), (5, 8, 2, 1), (130, 128, 256, 8)])
+                                     (4096, 1024, 16, 4), (5, 8, 2, 1), (130, 128, 256, 8),
+                                     (2000, 512, 36, 4), (600, 256, 128, 8), (300, 96, 24, 16),
+                                     (8192, 2048, 64, 8)])
 def test_router_topk_bit_exact(rb, orc, T, D, E, k):
     x = orc.to_bf16(orc.normal("moe_x", (T, D)))
     wr = orc.to_bf16(orc.normal("moe_router", (D, E), sigma=0.02))
