@@ -333,6 +333,20 @@ int remora_b200_moe_ep_down_bf16(const void* h, const void* wd, const int32_t* s
                                  int E, int64_t cap, int64_t F, int64_t D,
                                  const uint64_t* y_ptrs, void* stream);
 
+/* Steps 2 and 3 as one cooperative kernel: the copy warps of step 2, the
+ * SwiGLU tiles of step 2 and the down tiles of step 3 share one tile list in
+ * which the SwiGLU tiles of a group of 16 row tiles come before the down
+ * tiles of the previous group, so the down epilogues' NVLink stores overlap
+ * later SwiGLU tensor work.  A down tile waits (bounded) until every SwiGLU
+ * tile of its row tile is stored.  mt_done: local int32 scratch of
+ * P*cap/128 + E + 1 entries (zeroed by the call).  D and F multiples of 32. */
+int remora_b200_moe_ep_experts_fused_bf16(
+    const void* x, const int32_t* perm, const int32_t* offsets, int64_t n, int k, int64_t D,
+    int64_t F, int E, int P, int rank, int64_t cap, const uint64_t* recv_ptrs,
+    const uint64_t* ready_ptrs, const int32_t* ready_local, int32_t* done, int epoch,
+    const void* recv_local, const void* wg, const void* wu, const void* wd, void* h,
+    const int32_t* seg, int32_t* mt_done, const uint64_t* y_ptrs, void* stream);
+
 /* ------------------------------------------------------------------------
  * Seeded input generator (device side of the counter-based generator the
  * tests and benchmarks use; one stream key per tensor)

@@ -90,6 +90,8 @@ _SIGNATURES = {
     "remora_b200_moe_ep_dispatch_swiglu_bf16": ([P, P, P, I64, I, I64, I64, I, I, I, I64, P, P,
                                                  P, P, I, P, P, P, P, P, P], I),
     "remora_b200_moe_ep_down_bf16": ([P, P, P, I, I, I64, I64, I64, P, P], I),
+    "remora_b200_moe_ep_experts_fused_bf16": ([P, P, P, I64, I, I64, I64, I, I, I, I64, P, P, P,
+                                               P, I, P, P, P, P, P, P, P, P, P], I),
     "remora_b200_device_status": ([], I),
     "remora_b200_fill_normal": ([P, I64, I, U64, D, D, P], I),
     "remora_b200_fill_uniform": ([P, I64, I, U64, D, D, P], I),

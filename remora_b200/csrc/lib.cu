@@ -9,5 +9,6 @@
 #include "moe_gemm.cu"
 #include "moe_host.cu"
 #include "moe_noalloc.cu"
+#include "moe_ep_experts.cu"
 #include "moe_ep.cu"
 #include "dispatch.cu"

@@ -309,47 +309,72 @@ __global__ void __launch_bounds__(kDispThreads)
   }
 }
 
-// xs[pos, :] = x[perm[pos] / k, :]; one warp per row, 16-byte pieces.
+// xs[pos, :] = x[perm[pos] / k, :]; one warp per row, 16-byte pieces, up
+// to 8 pieces per lane loaded before they are stored (loads in flight).
 __global__ void k_gather_rows(const uint16_t* __restrict__ x, const int32_t* __restrict__ perm,
                               int64_t rows, int k, int D, uint16_t* __restrict__ xs) {
   const int lane = threadIdx.x & 31;
   const int64_t wpb = blockDim.x >> 5;
+  const int D8 = D / 8;
   for (int64_t row = blockIdx.x * wpb + (threadIdx.x >> 5); row < rows;
        row += (int64_t)gridDim.x * wpb) {
     const int64_t t = perm[row] / k;
     const uint4* src = reinterpret_cast<const uint4*>(x + t * D);
     uint4* dst = reinterpret_cast<uint4*>(xs + row * D);
-    for (int c = lane; c < D / 8; c += 32) dst[c] = __ldg(src + c);
+    for (int c0 = 0; c0 < D8; c0 += 8 * 32) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < D8) v[u] = __ldg(src + c);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < D8) dst[c] = v[u];
+      }
+    }
   }
 }
 
 // ----------------------------------------------------------------- combine
 // out[t, :] = bf16( (((0 + w0*y0) + w1*y1) + ...) ) in slot order, each
-// product and sum rounded separately as the reference ops are.
+// product and sum rounded separately as the reference ops are.  One warp
+// per token; KMAX >= k is a compile-time bound, so the slot rows and
+// weights sit in registers and, for each 16-byte column piece, the k row
+// loads are issued before the slot-order accumulation.
+template <int KMAX>
 __global__ void k_combine(const uint16_t* __restrict__ y, const int32_t* __restrict__ inv,
                           const float* __restrict__ w, int64_t T, int k, int D,
                           uint16_t* __restrict__ out) {
   const int lane = threadIdx.x & 31;
   const int64_t wpb = blockDim.x >> 5;
   for (int64_t t = blockIdx.x * wpb + (threadIdx.x >> 5); t < T; t += (int64_t)gridDim.x * wpb) {
-    int32_t rows[16];
-    float ws[16];
-    for (int j = 0; j < k; ++j) {
-      rows[j] = inv[t * k + j];
-      ws[j] = w[t * k + j];
+    const uint4* rows[KMAX];
+    float ws[KMAX];
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      rows[j] = reinterpret_cast<const uint4*>(y + (int64_t)(j < k ? inv[t * k + j] : 0) * D);
+      ws[j] = j < k ? w[t * k + j] : 0.0f;
     }
     for (int c = lane; c < D / 8; c += 32) {
+      uint4 v[KMAX];
+#pragma unroll
+      for (int j = 0; j < KMAX; ++j)
+        if (j < k) v[j] = __ldg(rows[j] + c);
       float acc[8];
 #pragma unroll
       for (int q = 0; q < 8; ++q) acc[q] = 0.0f;
-      for (int j = 0; j < k; ++j) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(y + (int64_t)rows[j] * D) + c);
-        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          acc[2 * q] = __fadd_rn(acc[2 * q], __fmul_rn(ws[j], __uint_as_float(u[q] << 16)));
-          acc[2 * q + 1] =
-              __fadd_rn(acc[2 * q + 1], __fmul_rn(ws[j], __uint_as_float(u[q] & 0xffff0000u)));
+      for (int j = 0; j < KMAX; ++j) {
+        if (j < k) {
+          const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            acc[2 * q] = __fadd_rn(acc[2 * q], __fmul_rn(ws[j], __uint_as_float(u[q] << 16)));
+            acc[2 * q + 1] =
+                __fadd_rn(acc[2 * q + 1], __fmul_rn(ws[j], __uint_as_float(u[q] & 0xffff0000u)));
+          }
         }
       }
       uint4 o;

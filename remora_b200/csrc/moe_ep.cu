@@ -352,3 +352,121 @@ extern "C" int remora_b200_moe_ep_down_bf16(const void* h, const void* wd, const
                         as_stream(stream), seg + 2 * S, S, seg, seg + S, seg + 3 * S,
                         seg + 4 * S, &yp);
 }
+
+// Fused path, steps 2 and 3 in one kernel: scatter + SwiGLU + down (see
+// moe_ep_experts.cu).  mt_done: [P*cap/128 + E + 1] int32 scratch (zeroed
+// here, stream-ordered).
+extern "C" int remora_b200_moe_ep_experts_fused_bf16(
+    const void* x, const int32_t* perm, const int32_t* offsets, int64_t n, int k, int64_t D,
+    int64_t F, int E, int P, int rank, int64_t cap, const uint64_t* recv_ptrs,
+    const uint64_t* ready_ptrs, const int32_t* ready_local, int32_t* done, int epoch,
+    const void* recv_local, const void* wg, const void* wu, const void* wd, void* h,
+    const int32_t* seg, int32_t* mt_done, const uint64_t* y_ptrs, void* stream) {
+  clear_error();
+  RB_CHECK_ARG(P >= 1 && P <= 8 && rank >= 0 && rank < P && E % P == 0 && E <= GMaxE,
+               "moe_ep_experts_fused: bad P=%d rank=%d E=%d", P, rank, E);
+  RB_CHECK_ARG(n >= 0 && n <= cap && k >= 1 && cap > 0 && D > 0 && F > 0 && D % 32 == 0 &&
+                   F % 32 == 0,
+               "moe_ep_experts_fused: bad sizes (D, F multiples of 32)");
+  RB_CHECK_ARG((int64_t)P * cap < (1ll << 31) && D < (1 << 30) && F < (1 << 30),
+               "moe_ep_experts_fused: sizes exceed 2^31");
+  RB_CHECK_ARG(offsets && ready_local && done && seg && mt_done && recv_local && wg && wu && wd &&
+                   h && (n == 0 || (x && perm)),
+               "moe_ep_experts_fused: null pointer");
+  RB_CHECK_ARG(aligned16(recv_local) && aligned16(wg) && aligned16(wu) && aligned16(wd) &&
+                   aligned16(h) && (n == 0 || aligned16(x)),
+               "moe_ep_experts_fused: pointers must be 16-byte aligned");
+  PeerPtrs rp, rdp, yp;
+  int rc;
+  if ((rc = peer_ptrs(recv_ptrs, P, &rp, "recv")) || (rc = peer_ptrs(ready_ptrs, P, &rdp, "ready")) ||
+      (rc = peer_ptrs(y_ptrs, P, &yp, "y")))
+    return rc;
+  const int Epr = E / P, S = E;
+  const int64_t rows = (int64_t)P * cap;
+  CUtensorMap tX, tG, tU, tH, tW;
+  {
+    uint64_t d[2] = {(uint64_t)D, (uint64_t)rows};
+    uint64_t st[1] = {(uint64_t)D * 2};
+    uint32_t box[2] = {GBK, GBM};
+    if ((rc = make_tmap(&tX, recv_local, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, st, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+  }
+  {
+    uint64_t d[2] = {(uint64_t)F, (uint64_t)rows};
+    uint64_t st[1] = {(uint64_t)F * 2};
+    uint32_t box[2] = {GBK, GBM};
+    if ((rc = make_tmap(&tH, h, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, st, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+  }
+  {
+    uint64_t d[3] = {(uint64_t)F, (uint64_t)D, (uint64_t)Epr};
+    uint64_t st[2] = {(uint64_t)F * 2, (uint64_t)D * F * 2};
+    uint32_t box[3] = {64, GBK, 1};
+    if ((rc = make_tmap(&tG, wg, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, d, st, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        (rc = make_tmap(&tU, wu, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, d, st, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+  }
+  {
+    uint64_t d[3] = {(uint64_t)D, (uint64_t)F, (uint64_t)Epr};
+    uint64_t st[2] = {(uint64_t)D * 2, (uint64_t)F * D * 2};
+    uint32_t box[3] = {64, GBK, 1};
+    if ((rc = make_tmap(&tW, wd, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, d, st, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+  }
+  ExpertsShape sh;
+  sh.D = (int)D;
+  sh.F = (int)F;
+  sh.E = Epr;
+  sh.S = S;
+  sh.tn_s = (int)((F + 127) / 128);
+  sh.tn_d = (int)((D + 255) / 256);
+  sh.kb_s = (int)((D + GBK - 1) / GBK);
+  sh.kb_d = (int)((F + GBK - 1) / GBK);
+  sh.seg_start = seg;
+  sh.seg_end = seg + S;
+  sh.seg_expert = seg + 2 * S;
+  sh.seg_dst_row = seg + 3 * S;
+  sh.seg_src = seg + 4 * S;
+  sh.h = static_cast<uint16_t*>(h);
+  sh.y = yp;
+  sh.ready = ready_local;
+  sh.epoch = epoch;
+  sh.mt_done = mt_done;
+  ScatterArgs sc;
+  sc.x = static_cast<const uint16_t*>(x);
+  sc.perm = perm;
+  sc.offsets = offsets;
+  sc.n = n;
+  sc.cap = cap;
+  sc.k = k;
+  sc.D = (int)D;
+  sc.Epr = Epr;
+  sc.P = P;
+  sc.rank = rank;
+  sc.epoch = epoch;
+  sc.recv = rp;
+  sc.ready = rdp;
+  sc.done = done;
+  RB_CUDA(cudaMemsetAsync(mt_done, 0, sizeof(int32_t) * (size_t)(rows / GBM + S + 1),
+                          as_stream(stream)));
+  constexpr int kSW = 2;
+  auto kern = k_ep_experts<kSW>;
+  RB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GSmemBytes));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms());
+  cfg.blockDim = dim3(GThreads + 32 * kSW);
+  cfg.dynamicSmemBytes = GSmemBytes;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  RB_CUDA(cudaLaunchKernelEx(&cfg, kern, tX, tG, tU, tH, tW, sh, sc));
+  return REMORA_B200_OK;
+}

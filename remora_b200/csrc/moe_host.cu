@@ -249,8 +249,17 @@ int combine_launch(const void* y, const int32_t* inv, const float* w, int64_t T,
                "combine: null or unaligned pointer");
   const int64_t want = (T + 7) / 8;
   const int64_t cap = (int64_t)num_sms() * 16;
-  k_combine<<<(unsigned)(want < cap ? want : cap), 256, 0, st>>>(
-      static_cast<const uint16_t*>(y), inv, w, T, k, (int)D, static_cast<uint16_t*>(out));
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  const uint16_t* yy = static_cast<const uint16_t*>(y);
+  uint16_t* oo = static_cast<uint16_t*>(out);
+  if (k <= 2)
+    k_combine<2><<<grid, 256, 0, st>>>(yy, inv, w, T, k, (int)D, oo);
+  else if (k <= 4)
+    k_combine<4><<<grid, 256, 0, st>>>(yy, inv, w, T, k, (int)D, oo);
+  else if (k <= 8)
+    k_combine<8><<<grid, 256, 0, st>>>(yy, inv, w, T, k, (int)D, oo);
+  else
+    k_combine<16><<<grid, 256, 0, st>>>(yy, inv, w, T, k, (int)D, oo);
   RB_LAUNCH_CHECK();
   return REMORA_B200_OK;
 }

@@ -82,6 +82,9 @@ class PeerEP:
         self.flags = view(self.off_flags, P, torch.int32)
         self.ready = view(self.off_ready, E, torch.int32)
         self.done = torch.zeros(E, dtype=torch.int32, device=self.device)
+        self.mt_done = torch.zeros(P * self.cap // 128 + E + 1, dtype=torch.int32,
+                                   device=self.device)
+        self.two_kernels = False  # True: scatter+SwiGLU and down as two launches
         self.meta = view(self.off_meta, P * (self.Epr + 1), torch.int32)
         self.recv = view(self.off_recv, P * cap * D, torch.bfloat16).view(P * cap, D)
         self.y = view(self.off_y, cap * D, torch.bfloat16).view(cap, D)
@@ -156,6 +159,23 @@ class PeerEP:
             self.done.data_ptr(), self.seg.data_ptr(), stream))
         mark("meta")
         self.layer += 1
+        if not self.two_kernels:
+            rb._check(L.remora_b200_moe_ep_experts_fused_bf16(
+                x.data_ptr(), perm.data_ptr(), offsets.data_ptr(), self.cap, self.k, self.D,
+                self.F, self.E, self.P, self.rank, self.cap, self.recv_ptrs, self.ready_ptrs,
+                self.ready.data_ptr(), self.done.data_ptr(), self.layer, self.recv.data_ptr(),
+                wg_local.contiguous().data_ptr(), wu_local.contiguous().data_ptr(),
+                wd_local.contiguous().data_ptr(), self.h.data_ptr(), self.seg.data_ptr(),
+                self.mt_done.data_ptr(), self.y_ptrs, stream))
+            mark("experts")
+            self._barrier(stream)
+            mark("barrier2")
+            out = rb.moe_combine(self.y, inv, w, out=out)
+            mark("combine")
+            if self.profile:
+                marks[-1][1].synchronize()
+                self.phase_ms = {b[0]: a[1].elapsed_time(b[1]) for a, b in zip(marks, marks[1:])}
+            return out
         rb._check(L.remora_b200_moe_ep_dispatch_swiglu_bf16(
             x.data_ptr(), perm.data_ptr(), offsets.data_ptr(), self.cap, self.k, self.D, self.F,
             self.E, self.P, self.rank, self.cap, self.recv_ptrs, self.ready_ptrs,

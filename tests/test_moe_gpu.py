@@ -87,8 +87,9 @@ def test_dispatch_rejects_bad_expert_id(rb):
     rb.synchronize_and_check()  # the error word was cleared
 
 
-def test_gather_and_combine_bit_exact(rb, orc):
-    T, D, E, k = 500, 256, 8, 2
+@pytest.mark.parametrize("T,D,E,k", [(500, 256, 8, 2), (300, 1000, 16, 5), (64, 2048, 64, 8),
+                                     (40, 136, 32, 12), (7, 8, 4, 3)])
+def test_gather_and_combine_bit_exact(rb, orc, T, D, E, k):
     x, wr, *_ = _moe_inputs(orc, T, D, 128, E)
     idx, w = orc.router_topk(x, wr, k)
     _, _, perm, inv = orc.dispatch(idx, E)
