@@ -310,36 +310,22 @@ int remora_b200_moe_ep_meta(const int32_t* offsets, int P, int E, int rank, int6
                             int32_t* flags, const uint64_t* flag_ptrs, int epoch,
                             int32_t* done, int32_t* seg, void* stream);
 
-/* Step 2: one cooperative kernel (one CTA per SM) whose extra warps copy
- * this rank's n dispatched rows into region `rank` of their owners' recv
- * (destinations in the order rank, rank+1, ...) and publish `epoch` (the
- * layer count, increasing) in the owner's ready slot of an expert once all
- * of the expert's rows are stored, while the tcgen05 pipeline runs the
- * SwiGLU grouped GEMM over the received segments (recv_local -> h
- * [P*cap, F]); a segment's first tile waits, bounded, for its ready slot.
- * REMORA_B200_EP_SCATTER_WARPS (2, 4 or 8; default 2) sets the copy warps
- * per CTA. */
-int remora_b200_moe_ep_dispatch_swiglu_bf16(
-    const void* x, const int32_t* perm, const int32_t* offsets, int64_t n, int k, int64_t D,
-    int64_t F, int E, int P, int rank, int64_t cap, const uint64_t* recv_ptrs,
-    const uint64_t* ready_ptrs, const int32_t* ready_local, int32_t* done, int epoch,
-    const void* recv_local, const void* wg, const void* wu, void* h, const int32_t* seg,
-    void* stream);
-
-/* Step 3: the down grouped GEMM over the same segments, each output row
- * stored into its source rank's y (followed by a barrier and the local
- * remora_b200_moe_combine_bf16). */
-int remora_b200_moe_ep_down_bf16(const void* h, const void* wd, const int32_t* seg, int P,
-                                 int E, int64_t cap, int64_t F, int64_t D,
-                                 const uint64_t* y_ptrs, void* stream);
-
-/* Steps 2 and 3 as one cooperative kernel: the copy warps of step 2, the
- * SwiGLU tiles of step 2 and the down tiles of step 3 share one tile list in
- * which the SwiGLU tiles of a group of 16 row tiles come before the down
- * tiles of the previous group, so the down epilogues' NVLink stores overlap
- * later SwiGLU tensor work.  A down tile waits (bounded) until every SwiGLU
- * tile of its row tile is stored.  mt_done: local int32 scratch of
- * P*cap/128 + E + 1 entries (zeroed by the call).  D and F multiples of 32. */
+/* Step 2: one cooperative kernel (one CTA per SM) that does the whole
+ * expert side.  Two extra warps per CTA copy this rank's n dispatched rows
+ * into region `rank` of their owners' recv (destinations in the order rank,
+ * rank+1, ...) and publish `epoch` (the layer count, increasing) in the
+ * owner's ready slot of an expert once all of the expert's rows are stored.
+ * The tcgen05 pipeline meanwhile runs two kinds of tile from one list:
+ * SwiGLU tiles over the received segments (recv_local -> h [P*cap, F]; a
+ * segment's first tile waits, bounded, for its ready slot) and down tiles
+ * (h -> the source rank's y over NVLink; a down tile waits, bounded, until
+ * every SwiGLU tile of its 128-row tile is stored).  The SwiGLU tiles of a
+ * group of 16 row tiles come before the down tiles of the previous group,
+ * so the down epilogues' NVLink stores overlap later SwiGLU tensor work.
+ * wg, wu [E/P, D, F], wd [E/P, F, D]: this rank's experts.  mt_done: local
+ * int32 scratch of P*cap/128 + E + 1 entries (zeroed by the call).  D and F
+ * multiples of 32.  Step 3 is remora_b200_moe_ep_barrier, then the local
+ * remora_b200_moe_combine_bf16 of y. */
 int remora_b200_moe_ep_experts_fused_bf16(
     const void* x, const int32_t* perm, const int32_t* offsets, int64_t n, int k, int64_t D,
     int64_t F, int E, int P, int rank, int64_t cap, const uint64_t* recv_ptrs,

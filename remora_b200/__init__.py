@@ -87,9 +87,6 @@ _SIGNATURES = {
     "remora_b200_moe_ep_segments": ([P, I, I, I64, P, P], I),
     "remora_b200_moe_ep_experts_bf16": ([P, P, P, P, P, P, I, I, I64, I64, I64, P, P], I),
     "remora_b200_moe_ep_meta": ([P, I, I, I, I64, P, P, P, P, I, P, P, P], I),
-    "remora_b200_moe_ep_dispatch_swiglu_bf16": ([P, P, P, I64, I, I64, I64, I, I, I, I64, P, P,
-                                                 P, P, I, P, P, P, P, P, P], I),
-    "remora_b200_moe_ep_down_bf16": ([P, P, P, I, I, I64, I64, I64, P, P], I),
     "remora_b200_moe_ep_experts_fused_bf16": ([P, P, P, I64, I, I64, I64, I, I, I, I64, P, P, P,
                                                P, I, P, P, P, P, P, P, P, P, P], I),
     "remora_b200_device_status": ([], I),

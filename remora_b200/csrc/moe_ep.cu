@@ -293,66 +293,6 @@ extern "C" int remora_b200_moe_ep_meta(const int32_t* offsets, int P, int E, int
   return REMORA_B200_OK;
 }
 
-// Fused path, step 2: one cooperative kernel per rank whose extra warps
-// scatter this rank's dispatched rows into the peers' recv buffers while its
-// tcgen05 pipeline runs the SwiGLU GEMM over the received segments, each
-// segment's first tile waiting (bounded) for its source's ready flag.
-extern "C" int remora_b200_moe_ep_dispatch_swiglu_bf16(
-    const void* x, const int32_t* perm, const int32_t* offsets, int64_t n, int k, int64_t D,
-    int64_t F, int E, int P, int rank, int64_t cap, const uint64_t* recv_ptrs,
-    const uint64_t* ready_ptrs, const int32_t* ready_local, int32_t* done, int epoch,
-    const void* recv_local, const void* wg, const void* wu, void* h, const int32_t* seg,
-    void* stream) {
-  clear_error();
-  RB_CHECK_ARG(P >= 1 && P <= 8 && rank >= 0 && rank < P && E % P == 0 && E <= GMaxE,
-               "moe_ep_dispatch_swiglu: bad P=%d rank=%d E=%d", P, rank, E);
-  RB_CHECK_ARG(n >= 0 && n <= cap && k >= 1 && D > 0 && D % 8 == 0 && F > 0 && cap > 0,
-               "moe_ep_dispatch_swiglu: bad sizes");
-  RB_CHECK_ARG((int64_t)P * cap < (1ll << 31), "moe_ep_dispatch_swiglu: P*cap exceeds 2^31 rows");
-  RB_CHECK_ARG(offsets && ready_local && done && seg && recv_local &&
-                   (n == 0 || (x && perm && aligned16(x))),
-               "moe_ep_dispatch_swiglu: null or unaligned pointer");
-  PeerPtrs rp, yp;
-  int rc;
-  if ((rc = peer_ptrs(recv_ptrs, P, &rp, "recv")) || (rc = peer_ptrs(ready_ptrs, P, &yp, "ready")))
-    return rc;
-  ScatterArgs sc;
-  sc.x = static_cast<const uint16_t*>(x);
-  sc.perm = perm;
-  sc.offsets = offsets;
-  sc.n = n;
-  sc.cap = cap;
-  sc.k = k;
-  sc.D = (int)D;
-  sc.Epr = E / P;
-  sc.P = P;
-  sc.rank = rank;
-  sc.epoch = epoch;
-  sc.recv = rp;
-  sc.ready = yp;
-  sc.done = done;
-  const int S = E;
-  return grouped_launch(true, recv_local, wg, wu, h, nullptr, (int64_t)P * cap, D, F, E / P,
-                        as_stream(stream), seg + 2 * S, S, seg, seg + S, nullptr, nullptr,
-                        nullptr, seg + 4 * S, ready_local, E / P, epoch, &sc);
-}
-
-// Fused path, step 3: the down GEMM over the same segments, every output
-// row stored into its source rank's y.
-extern "C" int remora_b200_moe_ep_down_bf16(const void* h, const void* wd, const int32_t* seg,
-                                            int P, int E, int64_t cap, int64_t F, int64_t D,
-                                            const uint64_t* y_ptrs, void* stream) {
-  clear_error();
-  RB_CHECK_ARG(P >= 1 && P <= 8 && E % P == 0 && E <= GMaxE && seg, "moe_ep_down: bad arguments");
-  PeerPtrs yp;
-  int rc;
-  if ((rc = peer_ptrs(y_ptrs, P, &yp, "y"))) return rc;
-  const int S = E;
-  return grouped_launch(false, h, wd, nullptr, nullptr, nullptr, (int64_t)P * cap, F, D, E / P,
-                        as_stream(stream), seg + 2 * S, S, seg, seg + S, seg + 3 * S,
-                        seg + 4 * S, &yp);
-}
-
 // Fused path, steps 2 and 3 in one kernel: scatter + SwiGLU + down (see
 // moe_ep_experts.cu).  mt_done: [P*cap/128 + E + 1] int32 scratch (zeroed
 // here, stream-ordered).

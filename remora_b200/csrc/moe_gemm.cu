@@ -50,14 +50,6 @@ struct GroupShape {
   const int32_t* seg_dst_row;
   const int32_t* seg_dst_rank;
   PeerPtrs dst;
-  // Optional readiness wait: before loading the first A tile of segment q
-  // the producer waits (bounded) until
-  //   wait_flags[seg_src[q] * wait_stride + seg_expert[q]] >= wait_epoch,
-  // i.e. until source rank seg_src[q] has stored every row of the segment.
-  const int32_t* seg_src;
-  const int32_t* wait_flags;
-  int wait_stride;
-  int wait_epoch;
 };
 
 // The expert-parallel dispatch carried by extra warps of the SwiGLU kernel:
@@ -245,10 +237,10 @@ __device__ __forceinline__ float silu_mul(float g, float u) {
   return (g * __frcp_rn(1.0f + e)) * u;
 }
 
-template <bool kSwiGLU, int kScatterWarps = 0>
-__global__ void __launch_bounds__(GThreads + 32 * kScatterWarps, 1)
+template <bool kSwiGLU>
+__global__ void __launch_bounds__(GThreads, 1)
     k_grouped_gemm(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
-                   const __grid_constant__ CUtensorMap tmB1, GroupShape s, ScatterArgs sc) {
+                   const __grid_constant__ CUtensorMap tmB1, GroupShape s) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -259,7 +251,6 @@ __global__ void __launch_bounds__(GThreads + 32 * kScatterWarps, 1)
   int* s_exp = s_en + (GMaxE + 1);
   int* s_drow = s_exp + (GMaxE + 1);
   int* s_drank = s_drow + (GMaxE + 1);
-  int* s_src = s_drank + (GMaxE + 1);
   // per epilogue warp: one [32 rows][128 B] staging tile, 1024-byte aligned
   uint8_t* epi_stage_base = smem + GEpiOffset;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -270,7 +261,6 @@ __global__ void __launch_bounds__(GThreads + 32 * kScatterWarps, 1)
       s_en[i] = s.seg_end[i];
       s_drow[i] = s.seg_dst_row ? s.seg_dst_row[i] : 0;
       s_drank[i] = s.seg_dst_rank ? s.seg_dst_rank[i] : 0;
-      s_src[i] = s.seg_src ? s.seg_src[i] : -1;
       const int e = s.seg_expert ? s.seg_expert[i] : i;
       s_exp[i] = (e >= 0 && e < s.E) ? e : 0;
       if (e < 0 || e >= s.E) atomicExch(&g_device_error, 2);
@@ -320,19 +310,6 @@ __global__ void __launch_bounds__(GThreads + 32 * kScatterWarps, 1)
       for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
         const TileInfo ti = group_tile(s, s_mt, s_st, s_en, s_exp, total_mt, t);
         const int n0 = ti.n * kColsPerTile;
-        if (s.wait_flags && s_src[ti.seg] >= 0) {
-          // s_src is read by this thread only: -1 marks a segment seen ready
-          const int flag = s_src[ti.seg] * s.wait_stride + s_exp[ti.seg];
-          if (!wait_flag_geq(s.wait_flags + flag, s.wait_epoch)) {
-            atomicExch(&g_device_error, 1);
-            *abort_flag = 1;
-            break;
-          }
-          // rows stored by other SMs / GPUs through the generic proxy are
-          // read below by TMA (the async proxy)
-          asm volatile("fence.proxy.async.global;" ::: "memory");
-          s_src[ti.seg] = -1;
-        }
         for (int kb = 0; kb < s.num_kb; ++kb) {
           if (!mbar_wait(&sm->empty[stage], phase ^ 1)) { *abort_flag = 1; break; }
           uint8_t* sa = smem + stage * GStageBytes;
@@ -402,10 +379,6 @@ __global__ void __launch_bounds__(GThreads + 32 * kScatterWarps, 1)
         mbar_wait(&sm->drain, 0);
       }
     }
-  } else if (warp >= 6) {
-    if (kScatterWarps > 0)
-      ep_scatter_warp(sc, (int64_t)blockIdx.x * kScatterWarps + (warp - 6),
-                      (int64_t)gridDim.x * kScatterWarps, lane);
   } else {
     const int lg = warp & 3;
     uint8_t* epi_stage = epi_stage_base + (warp - 2) * 32 * 128;

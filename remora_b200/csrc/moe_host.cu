@@ -127,27 +127,12 @@ int gather_launch(const void* x, const int32_t* perm, int64_t rows, int k, int64
 
 // Grouped GEMM over expert row segments.  a [rows, K]; b0 (and b1 for the
 // SwiGLU form) [E, K, N]; out [rows, N].  offsets [E+1] on the device.
-// Scatter warps per CTA of the fused dispatch + SwiGLU kernel: 2 (default),
-// 4 or 8, from REMORA_B200_EP_SCATTER_WARPS (read once).  Two keep the copy
-// ahead of the GEMM with the least interference (config 5 on 2 GPUs:
-// 2.74 ms for dispatch + SwiGLU with 2 warps, 2.69-2.83 with 4, 3.69 with 8).
-int scatter_warps() {
-  static int v = [] {
-    const char* e = getenv("REMORA_B200_EP_SCATTER_WARPS");
-    const int w = e ? atoi(e) : 2;
-    return (w == 4 || w == 8) ? w : 2;
-  }();
-  return v;
-}
-
 int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, void* out,
                    const int32_t* offsets, int64_t rows, int64_t K, int64_t N, int E,
                    cudaStream_t st, const int32_t* seg_expert = nullptr, int n_seg = -1,
                    const int32_t* seg_start = nullptr, const int32_t* seg_end = nullptr,
                    const int32_t* dst_row = nullptr, const int32_t* dst_rank = nullptr,
-                   const PeerPtrs* dst = nullptr, const int32_t* seg_src = nullptr,
-                   const int32_t* wait_flags = nullptr, int wait_stride = 1,
-                   int wait_epoch = 0, const ScatterArgs* scatter = nullptr) {
+                   const PeerPtrs* dst = nullptr) {
   const int cols = swiglu ? 128 : 256;
   const int S = n_seg < 0 ? E : n_seg;
   RB_CHECK_ARG(E >= 1 && E <= GMaxE, "grouped_gemm: E=%d unsupported (1..%d)", E, GMaxE);
@@ -157,9 +142,7 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
                (long long)N);
   RB_CHECK_ARG(rows < (1ll << 31) && K < (1ll << 31) && N < (1ll << 31),
                "grouped_gemm: sizes exceed 2^31");
-  if (rows == 0 && !scatter) return REMORA_B200_OK;
-  RB_CHECK_ARG(rows > 0, "grouped_gemm: the fused dispatch needs a non-empty receive buffer");
-  RB_CHECK_ARG(!scatter || swiglu, "grouped_gemm: the fused dispatch runs with the SwiGLU GEMM");
+  if (rows == 0) return REMORA_B200_OK;
   RB_CHECK_ARG(a && b0 && (out || dst) && (offsets || (seg_start && seg_end)) &&
                    (!swiglu || b1),
                "grouped_gemm: null pointer");
@@ -199,43 +182,18 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   sh.seg_dst_rank = dst ? dst_rank : nullptr;
   sh.dst = dst ? *dst : PeerPtrs{};
   sh.out = static_cast<uint16_t*>(out);
-  sh.seg_src = seg_src;
-  sh.wait_flags = wait_flags;
-  sh.wait_stride = wait_stride;
-  sh.wait_epoch = wait_epoch;
   // upper bound of the tile count: sum over experts of ceil(n_e / 128)
   const int64_t max_tiles = (rows / GBM + S) * (int64_t)sh.tiles_n;
   int grid = num_sms();
-  if (scatter) {
-    // every CTA carries scatter warps and the producers wait for rows that
-    // the scatter warps of other CTAs store: all CTAs must be resident at
-    // once, which a cooperative launch guarantees (or refuses to launch).
-    const int sw = scatter_warps();
-    auto kern = sw == 4 ? k_grouped_gemm<true, 4>
-                        : (sw == 8 ? k_grouped_gemm<true, 8> : k_grouped_gemm<true, 2>);
-    RB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GSmemBytes));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(GThreads + 32 * sw);
-    cfg.dynamicSmemBytes = GSmemBytes;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    RB_CUDA(cudaLaunchKernelEx(&cfg, kern, tA, tB0, tB1, sh, *scatter));
-    return REMORA_B200_OK;
-  }
   if (grid > max_tiles) grid = (int)max_tiles;
   if (swiglu) {
     RB_CUDA(cudaFuncSetAttribute(k_grouped_gemm<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  GSmemBytes));
-    k_grouped_gemm<true><<<grid, GThreads, GSmemBytes, st>>>(tA, tB0, tB1, sh, ScatterArgs{});
+    k_grouped_gemm<true><<<grid, GThreads, GSmemBytes, st>>>(tA, tB0, tB1, sh);
   } else {
     RB_CUDA(cudaFuncSetAttribute(k_grouped_gemm<false>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, GSmemBytes));
-    k_grouped_gemm<false><<<grid, GThreads, GSmemBytes, st>>>(tA, tB0, tB1, sh, ScatterArgs{});
+    k_grouped_gemm<false><<<grid, GThreads, GSmemBytes, st>>>(tA, tB0, tB1, sh);
   }
   RB_LAUNCH_CHECK();
   return REMORA_B200_OK;

@@ -9,13 +9,12 @@ default):
 
   router + top-k, dispatch over all E experts              (kernels)
   meta: counts -> every peer, barrier, segment table        (kernel, bounded)
-  dispatch + SwiGLU: one cooperative kernel; its scatter warps copy row p
-  into region r of rank (expert // Epr)'s recv and raise that rank's ready
-  flag when its rows are stored, while its tcgen05 pipeline computes the
-  SwiGLU GEMM over the received segments, sources in arrival order, each
-  waiting (bounded) for its source's flag                   (kernel, NVLink)
-  down grouped GEMM whose epilogue stores each output row
-  into its source rank's y                                  (kernel, NVLink)
+  experts: one cooperative kernel; its copy warps put row p into region r
+  of rank (expert // Epr)'s recv and raise that rank's ready flag of the
+  expert when its rows are stored, while its tcgen05 pipeline runs SwiGLU
+  tiles over the received segments (sources in arrival order, each
+  segment waiting, bounded, for its flag) and down tiles whose epilogues
+  store each output row into its source rank's y            (kernel, NVLink)
   barrier                                                   (kernel, bounded)
   combine of y in slot order                                (kernel)
 
@@ -84,7 +83,6 @@ class PeerEP:
         self.done = torch.zeros(E, dtype=torch.int32, device=self.device)
         self.mt_done = torch.zeros(P * self.cap // 128 + E + 1, dtype=torch.int32,
                                    device=self.device)
-        self.two_kernels = False  # True: scatter+SwiGLU and down as two launches
         self.meta = view(self.off_meta, P * (self.Epr + 1), torch.int32)
         self.recv = view(self.off_recv, P * cap * D, torch.bfloat16).view(P * cap, D)
         self.y = view(self.off_y, cap * D, torch.bfloat16).view(cap, D)
@@ -159,34 +157,14 @@ class PeerEP:
             self.done.data_ptr(), self.seg.data_ptr(), stream))
         mark("meta")
         self.layer += 1
-        if not self.two_kernels:
-            rb._check(L.remora_b200_moe_ep_experts_fused_bf16(
-                x.data_ptr(), perm.data_ptr(), offsets.data_ptr(), self.cap, self.k, self.D,
-                self.F, self.E, self.P, self.rank, self.cap, self.recv_ptrs, self.ready_ptrs,
-                self.ready.data_ptr(), self.done.data_ptr(), self.layer, self.recv.data_ptr(),
-                wg_local.contiguous().data_ptr(), wu_local.contiguous().data_ptr(),
-                wd_local.contiguous().data_ptr(), self.h.data_ptr(), self.seg.data_ptr(),
-                self.mt_done.data_ptr(), self.y_ptrs, stream))
-            mark("experts")
-            self._barrier(stream)
-            mark("barrier2")
-            out = rb.moe_combine(self.y, inv, w, out=out)
-            mark("combine")
-            if self.profile:
-                marks[-1][1].synchronize()
-                self.phase_ms = {b[0]: a[1].elapsed_time(b[1]) for a, b in zip(marks, marks[1:])}
-            return out
-        rb._check(L.remora_b200_moe_ep_dispatch_swiglu_bf16(
-            x.data_ptr(), perm.data_ptr(), offsets.data_ptr(), self.cap, self.k, self.D, self.F,
-            self.E, self.P, self.rank, self.cap, self.recv_ptrs, self.ready_ptrs,
+        rb._check(L.remora_b200_moe_ep_experts_fused_bf16(
+            x.data_ptr(), perm.data_ptr(), offsets.data_ptr(), self.cap, self.k, self.D,
+            self.F, self.E, self.P, self.rank, self.cap, self.recv_ptrs, self.ready_ptrs,
             self.ready.data_ptr(), self.done.data_ptr(), self.layer, self.recv.data_ptr(),
             wg_local.contiguous().data_ptr(), wu_local.contiguous().data_ptr(),
-            self.h.data_ptr(), self.seg.data_ptr(), stream))
-        mark("dispatch+swiglu")
-        rb._check(L.remora_b200_moe_ep_down_bf16(
-            self.h.data_ptr(), wd_local.contiguous().data_ptr(), self.seg.data_ptr(), self.P,
-            self.E, self.cap, self.F, self.D, self.y_ptrs, stream))
-        mark("down")
+            wd_local.contiguous().data_ptr(), self.h.data_ptr(), self.seg.data_ptr(),
+            self.mt_done.data_ptr(), self.y_ptrs, stream))
+        mark("experts")
         self._barrier(stream)
         mark("barrier2")
         out = rb.moe_combine(self.y, inv, w, out=out)
