@@ -576,11 +576,11 @@ def bench_moe_ep(args, world, rank, local):
     }
 
 
-# kernels of one EP layer: router 1, dispatch 3, then (fused) meta, dispatch+SwiGLU, down,
-# barrier, combine; (split) scatter, barrier, segments, SwiGLU, down, barrier, combine
-EP_LAUNCHES = {"p2p": 9, "p2p-split": 11, "nccl": 9}
-EP_MODES = {"p2p": "NVLink peer memory: scatter fused into the SwiGLU GEMM, down-GEMM epilogue "
-                   "stores to the source ranks",
+# kernels of one EP layer: router 1, dispatch 3, then (fused) meta, experts (copy + SwiGLU +
+# down), barrier, combine; (split) scatter, barrier, segments, SwiGLU, down, barrier, combine
+EP_LAUNCHES = {"p2p": 8, "p2p-split": 11, "nccl": 9}
+EP_MODES = {"p2p": "NVLink peer memory: row copy, SwiGLU and down tiles in one cooperative "
+                   "kernel, down epilogues store to the source ranks",
             "p2p-split": "NVLink peer memory: scatter kernel, barrier, GEMMs",
             "nccl": "NCCL all-to-all"}
 
