@@ -173,3 +173,46 @@ class PeerEP:
             marks[-1][1].synchronize()
             self.phase_ms = {b[0]: a[1].elapsed_time(b[1]) for a, b in zip(marks, marks[1:])}
         return out
+
+
+def _self_check(T=8192, D=2048, F=1536, E=8, k=8):
+    """One-rank run of the peer-memory layer (every row copied into the
+    rank's own region): four layers, a bit-for-bit comparison with the
+    single-GPU layer, then one layer with per-phase CUDA-event times.
+    ``python -m remora_b200.ep_p2p`` on one GPU."""
+    import datetime
+    import os
+
+    import remora_b200 as rb
+
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29533")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=0, world_size=1,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    x = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    wr = torch.empty(D, E, dtype=torch.bfloat16, device=dev)
+    ws = [torch.empty(s, dtype=torch.bfloat16, device=dev) for s in ((E, D, F), (E, D, F), (E, F, D))]
+    rb.fill_normal(x, rb.stream_key(30))
+    rb.fill_normal(wr, rb.stream_key(31), 0.0, 0.02)
+    for i, w in enumerate(ws):
+        rb.fill_normal(w, rb.stream_key(32 + i), 0.0, 0.02)
+    ep = PeerEP(T, D, F, E, k, device=dev)
+    ref = rb.moe_layer(x, wr, *ws, k)
+    for _ in range(4):
+        out = ep.forward(x, wr, *ws)
+    rb.synchronize_and_check(dev)
+    same = bool(torch.equal(out.view(torch.int16), ref.view(torch.int16)))
+    print("same as single-GPU layer:", same)
+    ep.profile = True
+    ep.forward(x, wr, *ws)
+    print({name: round(ms, 3) for name, ms in ep.phase_ms.items()})
+    dist.barrier()
+    dist.destroy_process_group()
+    if not same:
+        raise SystemExit(1)
+
+
+if __name__ == "__main__":
+    _self_check()
