@@ -55,3 +55,35 @@ def test_stream_keys_agree_with_oracle():
     for s in (1, 10, 34):
         for seed in (42, 7):
             assert rb.stream_key(s, seed) == oracle.stream_key(s, seed)
+
+
+def test_expert_parallel_entry_points_validate_before_cuda():
+    """Bad rank counts, sizes and null or misaligned peer addresses are
+    rejected on the host, before any CUDA call (works without a GPU)."""
+    import remora_b200 as rb
+
+    L = rb.lib()
+    P = 2
+    good = (ctypes.c_uint64 * P)(1 << 20, 2 << 20)
+    null = (ctypes.c_uint64 * P)(1 << 20, 0)
+    odd = (ctypes.c_uint64 * P)(1 << 20, (2 << 20) + 8)
+    buf = ctypes.create_string_buffer(4096)
+    p = ctypes.addressof(buf)
+
+    def experts(P_, rank, E, D, F, recv, ready, y, x=p):
+        return L.remora_b200_moe_ep_experts_fused_bf16(
+            x, p, p, 16, 2, D, F, E, P_, rank, 16, recv, ready, p, p, 1, p, p, p, p, p, p, p, y,
+            None)
+
+    assert experts(9, 0, 64, 256, 256, good, good, good) == rb.ERR_INVALID   # P > 8
+    assert experts(2, 2, 64, 256, 256, good, good, good) == rb.ERR_INVALID   # rank >= P
+    assert experts(2, 0, 63, 256, 256, good, good, good) == rb.ERR_INVALID   # E % P
+    assert experts(2, 0, 64, 200, 256, good, good, good) == rb.ERR_INVALID   # D % 32
+    assert experts(2, 0, 64, 256, 256, null, good, good) == rb.ERR_INVALID   # null peer
+    assert "null" in rb.last_error()
+    assert experts(2, 0, 64, 256, 256, good, good, odd) == rb.ERR_INVALID    # misaligned peer
+    assert experts(2, 0, 64, 256, 256, good, good, good, x=0) == rb.ERR_INVALID  # null x
+    rc = L.remora_b200_moe_ep_meta(p, P, 64, 5, 16, good, p, p, good, 1, p, p, None)
+    assert rc == rb.ERR_INVALID                                              # rank >= P
+    rc = L.remora_b200_moe_ep_barrier(p, null, P, 0, 1, None)
+    assert rc == rb.ERR_INVALID
