@@ -126,17 +126,19 @@ __device__ __forceinline__ int32_t* ep_ready_slot(const ScatterArgs& a, int e) {
   return reinterpret_cast<int32_t*>(a.ready.p[e / a.Epr]) + a.rank * a.Epr + e % a.Epr;
 }
 
-// Scatter warps of the fused dispatch + SwiGLU kernel (see ScatterArgs).
+// Copy warps of the expert-parallel expert kernel (see ScatterArgs).
 // Each warp copies chunks of two consecutive rows (16-byte pieces, up to 16
 // in flight per lane); chunks are spread over all scatter warps of the grid,
 // so the grid sweeps the rows in order and experts complete one after
 // another.  A warp counts the rows it stored per expert and keeps the
 // (expert, count) pairs it has finished in a pending list, one entry per
-// lane.  When kPending experts are pending (and at the end) it fences its
-// stores at system scope once and each pending lane adds its count to
+// lane.  When the list reaches its limit (and at the end) the warp fences
+// its stores at system scope once and each pending lane adds its count to
 // done[e]; the add that completes done[e] publishes the flag.  One fence
 // per kPending experts keeps the warp from waiting on NVLink
-// acknowledgements after every chunk.
+// acknowledgements after every chunk; the limit starts at 1 and doubles
+// after each flush, so the first experts' flags (the ones the GEMM needs
+// first) rise without waiting for later experts.
 constexpr int kPending = 4;
 
 __device__ __forceinline__ void ep_scatter_warp(const ScatterArgs& a, int64_t gw, int64_t GW,
@@ -154,6 +156,7 @@ __device__ __forceinline__ void ep_scatter_warp(const ScatterArgs& a, int64_t gw
   int cur = -1, cnt = 0;         // expert being copied, rows of it stored so far
   int pend_e = -1, pend_c = 0;    // this lane's entry of the pending list
   int npend = 0;                  // warp-uniform length of the pending list
+  int limit = 1;                  // warp-uniform: flush at this length
   auto flush = [&]() {
     if (npend == 0) return;
     __threadfence_system();
@@ -175,7 +178,10 @@ __device__ __forceinline__ void ep_scatter_warp(const ScatterArgs& a, int64_t gw
       pend_e = cur;
       pend_c = cnt;
     }
-    if (++npend == kPending) flush();
+    if (++npend >= limit) {
+      flush();
+      limit = min(2 * limit, kPending);
+    }
   };
   for (int64_t c = 2 * gw; c < n; c += 2 * GW) {
     const uint4* src[2];
