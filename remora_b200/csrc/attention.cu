@@ -2,8 +2,8 @@
 // mask]) V, on sm_100a tensor cores with fp32 softmax statistics.
 //
 // The reference has no attention program (README.md:12 lists FlashAttention
-// as in progress); the op is the BASELINE softmax attention over
-// Q, K, V bf16 [B, H, S, 128].
+// as in progress); the op is softmax attention, scale 1/sqrt(128), causal
+// or not, over Q, K, V bf16 [B, H, S, 128] (B=4, H=32, S=4096 at full size).
 //
 // One CTA per (batch*head, 256 query rows), 320 threads:
 //   warp 0      TMA producer: Q tiles once; K and V tiles of 128 rows into a

@@ -37,7 +37,7 @@ def test_scale_add_exp_parity(rb, orc, n):
     ref = orc.scale_add_exp(s, b, 0.125)
     out = rb.scale_add_exp(torch.from_numpy(s).cuda(), torch.from_numpy(b).cuda(), 0.125)
     got = out.cpu().numpy()
-    assert np.max(np.abs(got - ref) / np.abs(ref)) <= 1e-5  # BASELINE f32 tolerance
+    assert np.max(np.abs(got - ref) / np.abs(ref)) <= 1e-5  # f32 elementwise tolerance: 1e-5 relative
 
 
 def test_scale_add_exp_unaligned_views(rb, orc):
