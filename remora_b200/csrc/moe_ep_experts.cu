@@ -22,9 +22,12 @@
 // Warp roles as in k_grouped_gemm: TMA producer, MMA issuer, 4 epilogue
 // warps (TMEM accumulators double-buffered), then the scatter warps.
 #include "runtime.cuh"
+#include "ep_tiles.h"
 
 namespace rb {
 namespace moe {
+
+static_assert(GGroupM == kEpGroupM, "the tile order assumes groups of GGroupM row tiles");
 
 struct ExpertsShape {
   int D, F, E;                // model width, FFN width, experts on this rank
@@ -42,65 +45,6 @@ struct ExpertsShape {
   int epoch;                  // value the ready flags reach this layer
   int32_t* mt_done;           // [row tiles] zero at launch
 };
-
-struct XTile {
-  int down;  // 0: SwiGLU tile, 1: down tile
-  int m;     // 128-row tile
-  int n;     // column tile
-};
-
-// Tile t of the list S0 | S1 D0 | S2 D1 | ... | S_L D_{L-1} | D_L (S_g: the
-// SwiGLU tiles of row-tile group g, D_g its down tiles; every group but the
-// last holds GGroupM row tiles, row tile fastest within a block).
-__device__ __forceinline__ XTile x_tile(int t, int total_mt, int tn_s, int tn_d) {
-  const int G = (total_mt + GGroupM - 1) / GGroupM, L = G - 1;
-  const int gmL = total_mt - L * GGroupM;
-  const int fs = GGroupM * tn_s, fd = GGroupM * tn_d;
-  int down, g, rr, gm;
-  if (L == 0) {
-    down = t >= gmL * tn_s;
-    g = 0;
-    rr = down ? t - gmL * tn_s : t;
-    gm = gmL;
-  } else if (t < fs) {
-    down = 0;
-    g = 0;
-    rr = t;
-    gm = GGroupM;
-  } else {
-    const int u = t - fs, j = u / (fs + fd) + 1, r = u % (fs + fd);
-    if (j < L) {
-      down = r >= fs;
-      g = down ? j - 1 : j;
-      rr = down ? r - fs : r;
-      gm = GGroupM;
-    } else {
-      const int tp = t - (fs + (L - 1) * (fs + fd)), sL = gmL * tn_s;
-      if (tp < sL) {
-        down = 0; g = L; rr = tp; gm = gmL;
-      } else if (tp < sL + fd) {
-        down = 1; g = L - 1; rr = tp - sL; gm = GGroupM;
-      } else {
-        down = 1; g = L; rr = tp - sL - fd; gm = gmL;
-      }
-    }
-  }
-  XTile x;
-  x.down = down;
-  x.m = g * GGroupM + rr % gm;
-  x.n = rr / gm;
-  return x;
-}
-
-// Segment of row tile m: the last q with mt[q] <= m.
-__device__ __forceinline__ int seg_of_tile(const int* mt, int S, int m) {
-  int lo = 0, hi = S;
-  while (hi - lo > 1) {
-    const int mid = (lo + hi) >> 1;
-    if (mt[mid] <= m) lo = mid; else hi = mid;
-  }
-  return lo;
-}
 
 __device__ __forceinline__ bool wait_gpu_geq(const int32_t* f, int v) {
   const uint64_t t0 = globaltimer();
