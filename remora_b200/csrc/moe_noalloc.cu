@@ -25,7 +25,11 @@
 //     device address is looked up once per device with
 //     cudaGetSymbolAddress, with that device current.  The first call on a
 //     device performs this set-up; make that first call before any CUDA
-//     stream capture that might include it.
+//     stream capture that might include it.  The address belongs to the
+//     device's CUDA context: it is cached together with the context's
+//     unique id (cuCtxGetId), so after a cudaDeviceReset the next call sees
+//     a new context and looks the address up again (that call is then a
+//     first call again, with the same rule about stream capture).
 #include <mutex>
 
 #include "runtime.cuh"
@@ -38,25 +42,61 @@ constexpr int64_t kNoAllocScratchInts = 1 << 18;  // 1 MiB of int32 slots
 static __device__ __align__(256) int32_t g_noalloc_dispatch_scratch[kNoAllocScratchInts];
 
 constexpr int kMaxDevices = 64;
-static int32_t* g_noalloc_ptr[kMaxDevices] = {};
+struct NoAllocSlot {
+  int32_t* ptr;
+  unsigned long long ctx_id;  // unique id of the context the address belongs to
+};
+static NoAllocSlot g_noalloc[kMaxDevices] = {};
 static std::mutex g_noalloc_mu;
 
-// Device address of the scratch array on the current device (looked up
-// once per device).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id of the current thread's CUDA context (ids are never reused
+// within a process, unlike context handles).  0 when the driver cannot say.
+static unsigned long long current_ctx_id() {
+  static CtxGetCurrentFn get_cur = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (get_cur && get_id && get_cur(&c) == CUDA_SUCCESS && c && get_id(c, &id) == CUDA_SUCCESS)
+    return id;
+  return 0;
+}
+
+// Device address of the scratch array on the current device, looked up once
+// per device and context.  If the context id cannot be read, the address is
+// looked up on every call (cudaGetSymbolAddress allocates nothing).
 static int noalloc_scratch(int32_t** out) {
   int dev = 0;
   RB_CUDA(cudaGetDevice(&dev));
   RB_CHECK_ARG(dev >= 0 && dev < kMaxDevices, "dispatch_noalloc: device %d out of range", dev);
+  const unsigned long long ctx = current_ctx_id();
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  NoAllocSlot& slot = g_noalloc[dev];
+  if (!slot.ptr || ctx == 0 || slot.ctx_id != ctx) {
     int32_t* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_noalloc_dispatch_scratch);
     if (e != cudaSuccess || p == nullptr)
       return fail(REMORA_B200_ERR_CUDA, "dispatch_noalloc: cudaGetSymbolAddress failed: %s",
                   cudaGetErrorString(e));
-    g_noalloc_ptr[dev] = p;
+    slot.ptr = p;
+    // the lookup made the device's context current if no runtime call had
+    // yet on this thread: read its id now
+    slot.ctx_id = ctx ? ctx : current_ctx_id();
   }
-  *out = g_noalloc_ptr[dev];
+  *out = slot.ptr;
   return REMORA_B200_OK;
 }
 
@@ -70,6 +110,9 @@ extern "C" int remora_b200_moe_dispatch_noalloc(const int32_t* idx, int64_t T, i
   using namespace rb::moe;
   clear_error();
   RB_CHECK_ARG(T >= 0 && k >= 1 && E >= 1 && E <= GMaxE, "dispatch_noalloc: bad sizes");
+  RB_CHECK_ARG(T <= INT32_MAX / k,
+               "dispatch_noalloc: T*k = %lld*%d exceeds the int32 range of perm and inv",
+               (long long)T, k);
   RB_CHECK_ARG(T * k == 0 || (idx && counts && offsets && perm && inv),
                "dispatch_noalloc: null pointer");
   const int64_t need = dispatch_blocks(T * k) * (int64_t)E;
