@@ -267,6 +267,7 @@ extern "C" int remora_b200_moe_router_topk_bf16(const void* x, const void* wr, i
 }
 
 extern "C" size_t remora_b200_moe_dispatch_workspace_bytes(int64_t T, int k, int E) {
+  if (T < 0 || k < 1 || E < 1 || T > INT32_MAX / k) return 0;  // the dispatch rejects these
   return dispatch_ws_bytes(T, k, E);
 }
 
@@ -276,6 +277,9 @@ extern "C" int remora_b200_moe_dispatch(const int32_t* idx, int64_t T, int k, in
                                         void* stream) {
   clear_error();
   RB_CHECK_ARG(T >= 0 && k >= 1 && E >= 1 && E <= GMaxE, "dispatch: bad sizes");
+  RB_CHECK_ARG(T <= INT32_MAX / k,
+               "dispatch: T*k = %lld*%d exceeds the int32 range of perm and inv", (long long)T,
+               k);
   RB_CHECK_ARG(T * k == 0 || (idx && counts && offsets && perm && inv && workspace),
                "dispatch: null pointer");
   RB_CHECK_ARG(workspace_bytes >= dispatch_ws_bytes(T, k, E) || T * k == 0,
@@ -345,6 +349,7 @@ extern "C" int remora_b200_moe_layer_bf16(const void* x, const void* wr, const v
   clear_error();
   RB_CHECK_ARG(T >= 0 && D > 0 && F > 0 && E >= 1 && E <= GMaxE && k >= 1 && k <= 16 && k <= E,
                "moe_layer: bad sizes");
+  RB_CHECK_ARG(T <= INT32_MAX / k, "moe_layer: T*k exceeds the int32 range of the routing tables");
   if (T == 0) return REMORA_B200_OK;
   RB_CHECK_ARG(x && wr && wg && wu && wd && out && workspace, "moe_layer: null pointer");
   LayerWs L = layer_ws(workspace, T, D, F, E, k);
