@@ -257,12 +257,29 @@ int remora_b200_moe_layer_bf16(const void* x, const void* wr, const void* wg, co
  * Expert-parallel MoE over NVLink peer memory (P <= 8 ranks, one per GPU).
  * The reference has no multi-GPU path (one device, gpu_tests.cpp:102-104);
  * these replace an NCCL all-to-all for the token exchange.  Every rank holds
- * buffers its peers can address (e.g. torch symmetric memory): recv
+ * buffers its peers can address (remora_b200_peer_alloc below): recv
  * [P][cap][D] bf16, meta [P][E/P+1] int32, y [T_local*k][D] bf16 and flags
  * [P] int32 (zero-initialised once).  *_ptrs are host arrays of the P
  * ranks' device addresses of that buffer.  Only plain loads and stores
  * reach peer memory.
  * --------------------------------------------------------------------- */
+
+/* Peer-addressable buffers for the entry points below, one process per GPU.
+ * remora_b200_peer_alloc cudaMallocs `bytes` on the current device, zeroes
+ * them and writes the 64-byte CUDA IPC handle of the allocation to
+ * ipc_handle; the caller hands the handles to its peers (any channel: a
+ * process-group all-gather, MPI, a file) and each peer maps them with
+ * remora_b200_peer_open (cudaIpcOpenMemHandle with lazy peer access; the
+ * owner itself uses its own pointer).  Plain device memory: no NVLink
+ * multicast object is created, so a rank that exits leaves its peers only
+ * an unmapped range.  Teardown: every rank stops using the buffers (e.g. a
+ * barrier), closes the peers' mappings with remora_b200_peer_close, then
+ * frees its own with remora_b200_peer_free.  The reference has no
+ * counterpart (single device, compiler/gpu_tests.cpp:102-104). */
+int remora_b200_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int remora_b200_peer_open(const void* ipc_handle, void** ptr);
+int remora_b200_peer_close(void* ptr);
+int remora_b200_peer_free(void* ptr);
 
 /* Copies this rank's n dispatched rows (x[perm[p]/k], dispatch order of
  * remora_b200_moe_dispatch over all E experts) into region `rank` of the
@@ -332,6 +349,65 @@ int remora_b200_moe_ep_experts_fused_bf16(
     const uint64_t* ready_ptrs, const int32_t* ready_local, int32_t* done, int epoch,
     const void* recv_local, const void* wg, const void* wu, const void* wd, void* h,
     const int32_t* seg, int32_t* mt_done, const uint64_t* y_ptrs, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Expert-parallel MoE over NCCL (the all-to-all form).  One process or host
+ * thread per GPU; `comm` is an ncclComm_t (passed as void*) over the P ranks
+ * of the layer, created by the caller (or remora_b200_nccl_comm_init).
+ * NCCL is loaded at run time (libnccl.so.2, the copy the process already
+ * has if any), so the library has no link-time NCCL dependency.  The
+ * reference has no multi-GPU path (one device, compiler/gpu_tests.cpp:102-104);
+ * these serve the mixtral_moe_layer.mlir:8-68 program with its experts
+ * split over the ranks.
+ * --------------------------------------------------------------------- */
+
+/* Bytes of device workspace remora_b200_moe_ep_nccl_bf16 needs (0 for sizes
+ * it rejects).  Sized for the worst case: P*T*k rows may arrive. */
+size_t remora_b200_moe_ep_nccl_workspace_bytes(int64_t T, int64_t D, int64_t F, int E, int k,
+                                               int P);
+
+/* The whole layer on this rank: x bf16 [T, D] (this rank's tokens; every
+ * rank passes the same T), wr bf16 [D, E] (the full router), wg, wu bf16
+ * [E/P, D, F] and wd [E/P, F, D] (this rank's experts: global experts
+ * rank*E/P ...), out bf16 [T, D].  Router, dispatch and gather run locally;
+ * the per-expert counts and then the rows go to the experts' ranks by
+ * ncclSend/ncclRecv; the local grouped SwiGLU and down GEMMs run over the
+ * (source rank, local expert) segments; the outputs return the same way and
+ * are combined in slot order.  The result equals the single-GPU layer bit
+ * for bit.  The split sizes are read on the host once per call (2E+1
+ * int32), which synchronises `stream` once.  Host waits are bounded by
+ * timeout_ms (0 = 60 s): on expiry or on an NCCL error the communicator is
+ * aborted (ncclCommAbort, which ends its kernels) and the call returns
+ * REMORA_B200_ERR_TIMEOUT or REMORA_B200_ERR_NCCL.  Either code means the
+ * communicator has been aborted (and freed): do not use or destroy it again.  Works with blocking and non-blocking
+ * (config.blocking = 0) communicators.  D, F multiples of 32. */
+int remora_b200_moe_ep_nccl_bf16(const void* x, const void* wr, const void* wg, const void* wu,
+                                 const void* wd, void* out, int64_t T, int64_t D, int64_t F,
+                                 int E, int k, void* comm, int64_t timeout_ms, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+
+/* Host-side split bookkeeping of the exchange (no GPU needed): from this
+ * rank's dispatch offsets[E+1] and the received counts recv_counts[P][E/P]
+ * (rows source s routes to local expert e), the row block this rank sends
+ * to each rank q (send_off[q], send_rows[q]: dispatch rows of q's experts)
+ * and the block it receives from each (recv_off[q], recv_rows[q]: sources in
+ * rank order, each source's rows in local-expert order). */
+int remora_b200_moe_ep_splits(const int32_t* offsets, const int32_t* recv_counts, int P, int E,
+                              int64_t* send_off, int64_t* send_rows, int64_t* recv_off,
+                              int64_t* recv_rows);
+
+/* Communicator helpers for callers without their own NCCL bootstrap:
+ * rank 0 makes a 128-byte unique id and shares it with the others (any
+ * channel); every rank then calls remora_b200_nccl_comm_init with its
+ * device current.  blocking = 0 makes a non-blocking communicator whose
+ * initialisation is polled until timeout_ms (0 = 60 s), then aborted.
+ * remora_b200_nccl_comm_destroy finalises (bounded the same way) and frees;
+ * remora_b200_nccl_comm_abort ends a communicator at once. */
+int remora_b200_nccl_unique_id(void* id);
+int remora_b200_nccl_comm_init(void** comm, int nranks, const void* id, int rank, int blocking,
+                               int64_t timeout_ms);
+int remora_b200_nccl_comm_destroy(void* comm, int64_t timeout_ms);
+int remora_b200_nccl_comm_abort(void* comm);
 
 /* ------------------------------------------------------------------------
  * Seeded input generator (device side of the counter-based generator the

@@ -89,6 +89,18 @@ _SIGNATURES = {
     "remora_b200_moe_ep_meta": ([P, I, I, I, I64, P, P, P, P, I, P, P, P], I),
     "remora_b200_moe_ep_experts_fused_bf16": ([P, P, P, I64, I, I64, I64, I, I, I, I64, P, P, P,
                                                P, I, P, P, P, P, P, P, P, P, P], I),
+    "remora_b200_peer_alloc": ([ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), P], I),
+    "remora_b200_peer_open": ([P, ctypes.POINTER(ctypes.c_void_p)], I),
+    "remora_b200_peer_close": ([P], I),
+    "remora_b200_peer_free": ([P], I),
+    "remora_b200_moe_ep_nccl_workspace_bytes": ([I64, I64, I64, I, I, I], ctypes.c_size_t),
+    "remora_b200_moe_ep_nccl_bf16": ([P, P, P, P, P, P, I64, I64, I64, I, I, P, I64, P,
+                                      ctypes.c_size_t, P], I),
+    "remora_b200_moe_ep_splits": ([P, P, I, I, P, P, P, P], I),
+    "remora_b200_nccl_unique_id": ([P], I),
+    "remora_b200_nccl_comm_init": ([ctypes.POINTER(ctypes.c_void_p), I, P, I, I, I64], I),
+    "remora_b200_nccl_comm_destroy": ([P, I64], I),
+    "remora_b200_nccl_comm_abort": ([P], I),
     "remora_b200_device_status": ([], I),
     "remora_b200_fill_normal": ([P, I64, I, U64, D, D, P], I),
     "remora_b200_fill_uniform": ([P, I64, I, U64, D, D, P], I),

@@ -1,6 +1,6 @@
 // moe_ep.cu -- expert-parallel dispatch and combine over NVLink peer memory.
 //
-// Each rank owns, in memory every peer can address (symmetric buffers):
+// Each rank owns, in memory every peer can address (remora_b200_peer_alloc):
 //   recv  [P][cap][D] bf16  region s receives the rows rank s routes here
 //   meta  [P][Epr+1]  int32 region s: rows per local expert, then the row
 //                            of rank s's dispatch order they start at
@@ -408,5 +408,60 @@ extern "C" int remora_b200_moe_ep_experts_fused_bf16(
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   RB_CUDA(cudaLaunchKernelEx(&cfg, kern, tX, tG, tU, tH, tW, sh, sc));
+  return REMORA_B200_OK;
+}
+
+// ------------------------------------------------------------------------
+// Peer-addressable buffers.  Plain cudaMalloc memory shared through CUDA IPC:
+// no NVLink multicast object is created or bound, so a rank that exits (or
+// dies) leaves its peers' GPUs with nothing but an unmapped range.
+// ------------------------------------------------------------------------
+
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+
+extern "C" int remora_b200_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  clear_error();
+  RB_CHECK_ARG(bytes > 0 && ptr && ipc_handle, "peer_alloc: bad arguments");
+  void* p = nullptr;
+  RB_CUDA(cudaMalloc(&p, bytes));
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(REMORA_B200_ERR_CUDA, "peer_alloc: cudaIpcGetMemHandle: %s",
+                cudaGetErrorString(e));
+  }
+  e = cudaMemset(p, 0, bytes);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(REMORA_B200_ERR_CUDA, "peer_alloc: cudaMemset: %s", cudaGetErrorString(e));
+  }
+  memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return REMORA_B200_OK;
+}
+
+extern "C" int remora_b200_peer_open(const void* ipc_handle, void** ptr) {
+  clear_error();
+  RB_CHECK_ARG(ipc_handle && ptr, "peer_open: null argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  RB_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  *ptr = p;
+  return REMORA_B200_OK;
+}
+
+extern "C" int remora_b200_peer_close(void* ptr) {
+  clear_error();
+  RB_CHECK_ARG(ptr, "peer_close: null pointer");
+  RB_CUDA(cudaIpcCloseMemHandle(ptr));
+  return REMORA_B200_OK;
+}
+
+extern "C" int remora_b200_peer_free(void* ptr) {
+  clear_error();
+  if (!ptr) return REMORA_B200_OK;
+  RB_CUDA(cudaFree(ptr));
   return REMORA_B200_OK;
 }

@@ -2,10 +2,13 @@
 own kernels over NVLink peer memory (no NCCL in the layer, no host round
 trip for split sizes).
 
-Buffers every rank can address come from torch symmetric memory, allocated
-once per ``PeerEP`` (sized for the worst case: one rank may route all of
-its T_local*k rows to one peer).  One layer on rank r (``fused=True``, the
-default):
+Buffers every rank can address are plain ``cudaMalloc`` memory shared
+through CUDA IPC (``remora_b200_peer_alloc`` / ``remora_b200_peer_open``,
+handles exchanged over the process group), allocated once per ``PeerEP``
+and sized for the worst case: one rank may route all of its T_local*k rows
+to one peer.  No NVLink multicast object is created or bound, so a rank
+that exits leaves its peers nothing worse than an unmapped range.  One
+layer on rank r (``fused=True``, the default):
 
   router + top-k, dispatch over all E experts              (kernels)
   meta: counts -> every peer, barrier, segment table        (kernel, bounded)
@@ -37,11 +40,18 @@ def _align(n: int, a: int = 256) -> int:
     return (n + a - 1) // a * a
 
 
+class _DeviceRange:
+    """A raw device range as a torch tensor view (``__cuda_array_interface__``);
+    the memory stays owned by the PeerEP that allocated it."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
 class PeerEP:
     def __init__(self, T_local: int, D: int, F: int, E: int, k: int, group=None, device=None,
                  fused: bool = True):
-        import torch.distributed._symmetric_memory as symm_mem
-
         import remora_b200 as rb
 
         self.rb = rb
@@ -62,17 +72,26 @@ class PeerEP:
         self.off_recv = self.off_meta + _align(P * (self.Epr + 1) * 4)
         self.off_y = self.off_recv + _align(P * cap * D * 2)
         total = self.off_y + _align(cap * D * 2)
-        self.buf = symm_mem.empty(total, dtype=torch.uint8, device=self.device)
-        self.buf.zero_()
-        torch.cuda.synchronize(self.device)
-        gname = group.group_name if group is not None else dist.group.WORLD.group_name
-        if hasattr(symm_mem, "enable_symm_mem_for_group"):
-            try:
-                symm_mem.enable_symm_mem_for_group(gname)
-            except Exception:
-                pass
-        self.hdl = symm_mem.rendezvous(self.buf, gname)
-        base = list(self.hdl.buffer_ptrs)
+        L = rb.lib()
+        with torch.cuda.device(self.device):
+            own = ctypes.c_void_p()
+            handle = ctypes.create_string_buffer(64)
+            rb._check(L.remora_b200_peer_alloc(total, ctypes.byref(own), handle))  # zeroed
+            self._own = own.value
+            self._opened = []
+            handles = [None] * self.P
+            dist.all_gather_object(handles, handle.raw, group=group)
+            base = []
+            for r, hraw in enumerate(handles):
+                if r == self.rank:
+                    base.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                rb._check(L.remora_b200_peer_open(ctypes.create_string_buffer(hraw, 64),
+                                                  ctypes.byref(p)))
+                self._opened.append(p.value)
+                base.append(p.value)
+        self.buf = torch.as_tensor(_DeviceRange(self._own, total), device=self.device)
         arr = lambda off: (ctypes.c_uint64 * P)(*[b + off for b in base])
         self.flag_ptrs, self.meta_ptrs = arr(self.off_flags), arr(self.off_meta)
         self.ready_ptrs = arr(self.off_ready)
@@ -93,6 +112,42 @@ class PeerEP:
         self.profile = False   # when True, forward() records per-phase CUDA events
         self.phase_ms = {}
         dist.barrier(group)
+
+    def close(self):
+        """Releases the peer buffers: every rank finishes its work, unmaps its
+        peers' buffers, and only then frees its own (two barriers)."""
+        if self._own is None:
+            return
+        L = self.rb.lib()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                self.rb._check(L.remora_b200_peer_close(p))
+        self._opened = []
+        dist.barrier(self.group)
+        self.flags = self.ready = self.meta = self.recv = self.y = self.buf = None
+        with torch.cuda.device(self.device):
+            self.rb._check(L.remora_b200_peer_free(self._own))
+        self._own = None
+
+    @property
+    def dominant_kernel(self) -> str:
+        return ("rb::moe::k_ep_experts (row copy + SwiGLU + down, cooperative)" if self.fused
+                else "rb::moe::k_grouped_gemm (SwiGLU + down over received segments)")
+
+    @property
+    def launches_per_layer(self) -> int:
+        """The library's kernels in one forward(): router 1, dispatch 3, then
+        meta, experts, barrier, combine (fused) or scatter, barrier,
+        segments, SwiGLU, down, barrier, combine (split)."""
+        return 8 if self.fused else 11
+
+    def rows_received(self) -> int:
+        """Rows this rank's experts processed in the last layer (synchronises)."""
+        torch.cuda.synchronize(self.device)
+        m = self.meta.view(self.P, self.Epr + 1)[:, :self.Epr]
+        return int(m.sum().item())
 
     def _barrier(self, stream):
         self.epoch += 1
@@ -175,44 +230,54 @@ class PeerEP:
         return out
 
 
-def _self_check(T=8192, D=2048, F=1536, E=8, k=8):
-    """One-rank run of the peer-memory layer (every row copied into the
-    rank's own region): four layers, a bit-for-bit comparison with the
-    single-GPU layer, then one layer with per-phase CUDA-event times.
-    ``python -m remora_b200.ep_p2p`` on one GPU."""
+def _self_check(T=8192, D=2048, F=1536, E=8, k=8, port=29533):
+    """One-rank run of the peer-memory layer (every row goes to the rank's
+    own region): for the fused and the split form, three consecutive layers
+    on two different inputs, each compared bit for bit with the single-GPU
+    layer, then one layer with per-phase CUDA-event times.  The default
+    shape is one rank's share of the 65536-token, 64-expert configuration
+    on 8 GPUs (8192 tokens, 8 experts).  ``python -m remora_b200.ep_p2p`` on
+    one GPU; exits 1 on a mismatch."""
     import datetime
     import os
 
     import remora_b200 as rb
 
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    os.environ.setdefault("MASTER_PORT", "29533")
+    os.environ.setdefault("MASTER_PORT", str(port))
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", rank=0, world_size=1,
-                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    dist.init_process_group("gloo", rank=0, world_size=1,
+                            timeout=datetime.timedelta(seconds=60))
     x = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    x2 = torch.empty_like(x)
     wr = torch.empty(D, E, dtype=torch.bfloat16, device=dev)
     ws = [torch.empty(s, dtype=torch.bfloat16, device=dev) for s in ((E, D, F), (E, D, F), (E, F, D))]
     rb.fill_normal(x, rb.stream_key(30))
+    rb.fill_normal(x2, rb.stream_key(35))
     rb.fill_normal(wr, rb.stream_key(31), 0.0, 0.02)
     for i, w in enumerate(ws):
         rb.fill_normal(w, rb.stream_key(32 + i), 0.0, 0.02)
-    ep = PeerEP(T, D, F, E, k, device=dev)
-    ref = rb.moe_layer(x, wr, *ws, k)
-    for _ in range(4):
-        out = ep.forward(x, wr, *ws)
-    rb.synchronize_and_check(dev)
-    same = bool(torch.equal(out.view(torch.int16), ref.view(torch.int16)))
-    print("same as single-GPU layer:", same)
-    ep.profile = True
-    ep.forward(x, wr, *ws)
-    print({name: round(ms, 3) for name, ms in ep.phase_ms.items()})
-    dist.barrier()
+    refs = [rb.moe_layer(xi, wr, *ws, k) for xi in (x, x2)]
+    ok = True
+    for fused in (True, False):
+        ep = PeerEP(T, D, F, E, k, device=dev, fused=fused)
+        outs = [ep.forward(xi, wr, *ws).clone() for xi in (x, x2, x)]
+        rb.synchronize_and_check(dev)
+        same = all(torch.equal(o.view(torch.int16), r.view(torch.int16))
+                   for o, r in zip(outs, (refs[0], refs[1], refs[0])))
+        ep.profile = True
+        ep.forward(x, wr, *ws)
+        print(f"{'fused' if fused else 'split'}: same as single-GPU layer: {same};",
+              {name: round(ms, 3) for name, ms in ep.phase_ms.items()}, flush=True)
+        ep.close()
+        ok = ok and same
     dist.destroy_process_group()
-    if not same:
+    if not ok:
         raise SystemExit(1)
 
 
 if __name__ == "__main__":
-    _self_check()
+    import sys
+
+    _self_check(port=int(sys.argv[1]) if len(sys.argv) > 1 else 29533)
