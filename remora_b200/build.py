@@ -42,7 +42,7 @@ def needs_build() -> bool:
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not needs_build():
         return LIB
-    cmd = [NVCC, *NVCC_FLAGS, os.path.join(CSRC, "lib.cu"), "-o", LIB + ".tmp", "-lcudart"]
+    cmd = [NVCC, *NVCC_FLAGS, os.path.join(CSRC, "lib.cu"), "-o", LIB + ".tmp", "-lcudart", "-ldl"]
     env = dict(os.environ)
     env.pop("CC", None)
     env.pop("CXX", None)
