@@ -1,18 +1,28 @@
 """Benchmark of the remora_b200 hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload gemm|elementwise]
+                    [--workload moe_ep|moe|gemm|attention|elementwise]
 
-Default workload (the headline config): stablehlo.dot_general GEMM, bf16
-A [8192,8192] x B [8192,8192] -> bf16, fp32 accumulate, U(-1,1) seeded
-inputs.  Under torchrun with N > 1 GPUs the workload is the batched form
-[8,4096,4096] x [8,4096,4096] with the batch split across ranks (no
-collective; the same 1.0995e12 FLOP per step in total, strong scaling).
-One step = one GEMM over the whole job's batch.  Rank 0 prints one JSON line.
+Default workload: the expert-parallel MoE layer, 65536 tokens x d_model 2048
+bf16, router [2048,64] with top-8 gating, 64 SwiGLU experts of ffn dim 1536,
+metric tokens/s.  With N = 1 one GPU runs the whole layer
+(remora_b200_moe_layer_bf16); under torchrun with N > 1 the tokens and the
+experts are split over the ranks (65536/N tokens and 64/N experts per GPU)
+and the token exchange runs over NVLink peer memory inside the library's
+expert kernel (remora_b200/ep_p2p.py).  The job's total work is fixed, so
+the scaling is strong.  Rank 0 prints one JSON line.
 
---impl reference times the reference's CPU path for the same metric: the C
-restatement of remora's convert-linalg-to-loops loop nest (oracle/), on all
-host threads, over a bounded row sample of the same GEMM per step.
+Other workloads: `moe` (one GPU per rank runs a whole layer: --moe-config 4
+= 8192 x 4096, 8 experts of F 14336, top-2; 5 = the default shape), `gemm`
+(dot_general bf16 8192^3; batch-sharded [8,4096,4096]^2 at N > 1),
+`attention` (causal [4,32,4096,128], (batch, head) pairs sharded) and
+`elementwise` (exp(s*0.125+b) f32 over 2^28 elements).
+
+--impl reference times the reference's CPU path for the same workload and
+metric: the C restatement of remora's loop nests (oracle/) on all host
+threads, one bounded sample of the workload per step.  `cpu_baseline` in the
+GPU arm's line is the same restatement timed single-threaded (the reference
+CPU path is scalar and single-threaded) and on all host threads.
 """
 from __future__ import annotations
 
@@ -29,6 +39,8 @@ import numpy as np
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+# NVLS (NVLink SHARP) binds NVLink multicast memory; nothing here needs it.
+os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
 
 METRIC = "MoE layer tokens/s; GEMM/attn TFLOP/s as % B200 peak; elementwise HBM GB/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -39,6 +51,14 @@ NCU_TRAFFIC_BYTES = {
     "gemm_8192": 1140578560,  # profiles/gemm_bf16_8192_dram.md
     "gemm_batched": None,
     "elementwise": None,
+    "moe_swiglu_5": None,
+    "moe_swiglu_4": None,
+    "moe_ep_experts": None,
+}
+
+MOE_CONFIGS = {
+    "4": dict(T=8192, D=4096, F=14336, E=8, k=2),
+    "5": dict(T=65536, D=2048, F=1536, E=64, k=8),
 }
 
 
@@ -130,12 +150,9 @@ def dist_setup(args):
         import torch
         import torch.distributed as dist
 
-        if args.impl == "ours":
-            torch.cuda.set_device(local)
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                    device_id=torch.device("cuda", local))
-        else:
-            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
     return world, rank, local
 
 
@@ -171,124 +188,227 @@ def barrier(world: int):
 
 
 # ------------------------------------------------------------- CPU timing
-_CPU_INPUTS: dict = {}
+# The reference CPU path (remora's ExecutionEngine over convert-linalg-to-loops
+# scalar loops, compiler/cpu.cpp:25-92) cannot be built offline; its loop
+# nests are restated in oracle/oracle.c, which is timed here on bounded
+# samples of each workload.  Each sampler returns (units done, seconds) for
+# one call of `chunk` units; rates are units per second.
+_CPU_CACHE: dict = {}
 
 
-def cpu_gemm_rows_rate(rows_per_call: int, budget_s: float, threads: int):
-    """Times the oracle's bf16 GEMM loop nest on rows of the 8192^3 problem.
-
-    Returns (TFLOP/s, rows timed, seconds).  The rows are the first rows of
-    the same seeded A, the full seeded B.
-    """
+def _oracle(threads: int):
     import oracle
 
     oracle.set_threads(threads)
-    K = N = 8192
-    key = ("gemm", rows_per_call)
-    if key not in _CPU_INPUTS:
-        _CPU_INPUTS.clear()
-        b = oracle.to_bf16(oracle.uniform("gemm_b", (K, N)))
-        a_rows = oracle.to_bf16(oracle.uniform("gemm_a", (rows_per_call * 4, K)))
-        _CPU_INPUTS[key] = (a_rows, b)
-    a_rows, b = _CPU_INPUTS[key]
-    done, t0 = 0, time.perf_counter()
+    return oracle
+
+
+def _gemm_sampler(threads):
+    """Output rows of the 8192^3 bf16 GEMM (the oracle's increasing-k fp32
+    loop nest); unit = FLOP (2*N*K per row)."""
+    orc = _oracle(threads)
+    if "gemm" not in _CPU_CACHE:
+        b = orc.to_bf16(orc.uniform("gemm_b", (8192, 8192)))
+        a = orc.to_bf16(orc.uniform("gemm_a", (256, 8192)))  # first rows of A
+        _CPU_CACHE["gemm"] = (a, b)
+    a, b = _CPU_CACHE["gemm"]
+    state = {"r": 0}
+
+    def run(chunk):
+        r0 = state["r"] % (a.shape[0] - chunk + 1)
+        orc.gemm_bf16_rows(a, b, r0, r0 + chunk)
+        state["r"] += chunk
+        return 2.0 * chunk * 8192 * 8192
+
+    return run, "output rows of the 8192^3 bf16 GEMM (oracle/oracle.c orc_gemm_bf16_rows)"
+
+
+def _moe_sampler(threads, cfg):
+    """Whole tokens of the MoE layer: router + top-k over all experts,
+    dispatch, the SwiGLU expert FFN of each routed row, combine (the oracle's
+    loop nests).  Every routed row runs through the first expert's weights:
+    the work per row is the same for every expert, and this keeps the sample
+    from generating all expert weights.  unit = tokens."""
+    orc = _oracle(threads)
+    c = MOE_CONFIGS[cfg]
+    T, D, F, E, k = c["T"], c["D"], c["F"], c["E"], c["k"]
+    key = ("moe", cfg)
+    if key not in _CPU_CACHE:
+        pool = 256
+        x = orc.to_bf16(orc.normal("moe_x", (pool, D)))  # the first token rows of x
+        wr = orc.to_bf16(orc.normal("moe_router", (D, E), sigma=0.02))
+        wg = orc.to_bf16(orc.normal("moe_wg", (D, F), sigma=0.02))
+        wu = orc.to_bf16(orc.normal("moe_wu", (D, F), sigma=0.02))
+        wd = orc.to_bf16(orc.normal("moe_wd", (F, D), sigma=0.02))
+        _CPU_CACHE[key] = (x, wr, wg, wu, wd)
+    x, wr, wg, wu, wd = _CPU_CACHE[key]
+    state = {"t": 0}
+
+    def run(chunk):
+        t0 = state["t"] % (x.shape[0] - chunk + 1)
+        xs = x[t0:t0 + chunk]
+        idx, w = orc.router_topk(xs, wr, k)
+        _, _, perm, inv = orc.dispatch(idx, E)
+        _, y, _ = orc.expert_ffn(np.ascontiguousarray(xs[perm // k]), wg, wu, wd)
+        orc.combine(y, inv, w)
+        state["t"] += chunk
+        return float(chunk)
+
+    return run, (f"whole tokens of the MoE layer T={T} D={D} F={F} E={E} top-{k} (router, "
+                 f"dispatch, SwiGLU FFN of every routed row, combine; oracle/oracle.c)")
+
+
+def _attention_sampler(threads):
+    """Query rows of one (batch, head) of causal [4,32,4096,128] attention
+    (the oracle's fp64 softmax restatement), rows drawn uniformly so the
+    average causal work matches the whole problem; unit = FLOP
+    (4*(row+1)*128 per row)."""
+    orc = _oracle(threads)
+    S, Dh = 4096, 128
+    if "attn" not in _CPU_CACHE:
+        _CPU_CACHE["attn"] = tuple(orc.to_bf16(orc.normal(n, (S, Dh)))
+                                   for n in ("attn_q", "attn_k", "attn_v"))
+    q, k, v = _CPU_CACHE["attn"]
+    rng = np.random.default_rng(7)
+
+    def run(chunk):
+        rows = rng.integers(0, S, chunk)
+        orc.attention_rows(q, k, v, rows, causal=True)
+        return float(np.sum(4.0 * (rows + 1) * Dh))
+
+    return run, "query rows of causal attention [4,32,4096,128] (oracle/oracle.c, fp64 softmax)"
+
+
+def _elementwise_sampler(threads):
+    """exp(s*0.125 + b) over f32 elements (the oracle's loop); unit = bytes
+    (12 per element: two reads, one write)."""
+    orc = _oracle(threads)
+    n = 1 << 22
+    if "ew" not in _CPU_CACHE:
+        _CPU_CACHE["ew"] = (orc.normal("scores", (n,)), orc.normal("bias", (n,)))
+    s, b = _CPU_CACHE["ew"]
+
+    def run(chunk):
+        m = min(chunk, n)
+        orc.scale_add_exp(s[:m], b[:m], 0.125)
+        return 12.0 * m
+
+    return run, "f32 elements of exp(s*0.125+b) (oracle/oracle.c)"
+
+
+CPU_UNITS = {"gemm": ("TFLOP/s", 1e12), "attention": ("TFLOP/s", 1e12), "moe": ("tokens/s", 1.0),
+             "moe_ep": ("tokens/s", 1.0), "elementwise": ("GB/s", 1e9)}
+
+
+def cpu_sampler(workload: str, threads: int, moe_cfg: str = "5"):
+    if workload == "gemm":
+        return _gemm_sampler(threads)
+    if workload in ("moe", "moe_ep"):
+        return _moe_sampler(threads, "5" if workload == "moe_ep" else moe_cfg)
+    if workload == "attention":
+        return _attention_sampler(threads)
+    return _elementwise_sampler(threads)
+
+
+def _chunk(workload: str, threads: int) -> int:
+    """Units per sampler call: enough parallel work for `threads` threads."""
+    tokens = 1 if threads == 1 else -(-threads // 4)  # k >= 2 routed rows per token
+    return {"gemm": threads, "moe": tokens, "moe_ep": tokens, "attention": 4 * threads,
+            "elementwise": 1 << 22}[workload]
+
+
+def cpu_rate(workload: str, threads: int, budget_s: float, moe_cfg: str = "5"):
+    """(rate in the workload's unit, units done, seconds, sample text)."""
+    run, what = cpu_sampler(workload, threads, moe_cfg)
+    chunk = _chunk(workload, threads)
+    run(chunk)  # warm-up (page-in, thread pool)
+    done, t0 = 0.0, time.perf_counter()
+    calls = 0
     while True:
-        r0 = (done % (rows_per_call * 4))
-        oracle.gemm_bf16_rows(a_rows, b, r0, r0 + rows_per_call)
-        done += rows_per_call
+        done += run(chunk)
+        calls += 1
         el = time.perf_counter() - t0
         if el >= budget_s:
             break
-    return 2.0 * done * N * K / el / 1e12, done, el
+    unit, scale = CPU_UNITS[workload]
+    return done / el / scale, calls * chunk, el, what
 
 
-def cpu_baseline_gemm(budget_s: float = 12.0):
-    import oracle
-
+def cpu_baseline(workload: str, moe_cfg: str = "5", budget_s: float = 8.0):
+    """The oracle restatement timed on this host: all threads (the line's
+    value) and one thread (the reference CPU path is single-threaded)."""
     threads = os.cpu_count() or 1
-    rate, rows, el = cpu_gemm_rows_rate(max(threads, 1), budget_s, threads)
-    return {"value": rate, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{rows} output rows of the 8192^3 bf16 GEMM (oracle/oracle.c "
-                      f"orc_gemm_bf16_rows, gcc -O2 -fopenmp, {threads} threads), {el:.1f} s"}
+    unit = CPU_UNITS[workload][0]
+    v1, n1, e1, what = cpu_rate(workload, 1, budget_s, moe_cfg)
+    vn, nn, en, _ = cpu_rate(workload, threads, budget_s, moe_cfg)
+    return {"value": vn, "unit": unit, "cores": threads, "kind": "port",
+            "sample": f"{nn} {what} on {threads} threads (gcc -O2 -fopenmp), {en:.1f} s",
+            "single_thread": {"value": v1, "unit": unit, "cores": 1,
+                              "sample": f"{n1} {what} on 1 thread, {e1:.1f} s"}}
 
 
-def cpu_baseline_moe(cfg: str, sample_rows: int = 0):
-    """Oracle MoE layer on the host: routing and dispatch of every token, then
-    the SwiGLU expert FFN on a sample of routed rows (all through one
-    expert's weights -- the work per row is the same for every expert) and
-    the combine; tokens/s extrapolated to the whole batch."""
-    import oracle
+# ------------------------------------------------------------ workloads
+def workload_config(args, world: int) -> dict:
+    """The workload's identity, the same in both arms' JSON lines."""
+    w = args.workload
+    if w == "moe_ep":
+        c = MOE_CONFIGS["5"]
+        T, E = c["T"], c["E"]
+        par = ("single GPU" if world == 1 else
+               f"expert-parallel x{world}: {T // world} tokens and {E // world} experts per GPU, "
+               f"{EP_MODES[args.ep_mode]}")
+        return {"workload": f"MoE layer: {T} tokens x d_model {c['D']} bf16, router "
+                            f"[{c['D']},{E}] top-{c['k']}, {E} SwiGLU experts of ffn dim {c['F']}",
+                **c, "parallelism": par,
+                "l2": "per-step working set (tokens, expert weights, dispatched rows) > 126 MB "
+                      "L2 (no flush)"}
+    if w == "moe":
+        c = MOE_CONFIGS[args.moe_config]
+        return {"workload": f"MoE layer config {args.moe_config}: T={c['T']} D={c['D']} "
+                            f"F={c['F']} E={c['E']} top-{c['k']}, SwiGLU experts", **c,
+                "parallelism": f"one whole layer per GPU x{world}" if world > 1 else "single GPU",
+                "l2": "weights and activations > 126 MB L2 (no flush)"}
+    if w == "gemm":
+        if args.size:
+            n = args.size
+            return {"workload": f"dot_general bf16 [{n},{n}]x[{n},{n}] (profiling case)",
+                    "M": n, "N": n, "K": n, "batch": 1, "parallelism": "single GPU"}
+        if world == 1:
+            return {"workload": "dot_general bf16 [8192,8192]x[8192,8192]->[8192,8192], fp32 "
+                                "accumulate", "M": 8192, "N": 8192, "K": 8192, "batch": 1,
+                    "parallelism": "single GPU",
+                    "l2": "inputs 256 MiB > 126 MB L2 (no flush)"}
+        return {"workload": "dot_general bf16 batched [8,4096,4096]x[8,4096,4096], fp32 "
+                            "accumulate", "M": 4096, "N": 4096, "K": 4096, "batch": 8,
+                "parallelism": f"batch-sharded x{world} ({8 // world} per GPU)",
+                "l2": "inputs > 126 MB L2 per GPU (no flush)"}
+    if w == "attention":
+        return {"workload": "causal softmax attention bf16 [4,32,4096,128], fp32 softmax "
+                            "statistics", "B": 4, "H": 32, "S": 4096, "Dh": 128, "causal": True,
+                "flop_convention": "4*B*H*S^2*Dh/2 (causal half)",
+                "parallelism": (f"(batch, head) pairs sharded x{world}" if world > 1
+                                else "single GPU"),
+                "l2": "q, k, v 402 MB > 126 MB L2 (no flush)"}
+    return {"workload": "exp(s*0.125+b) f32, 2^28 elements (3 GiB per step)", "n": 1 << 28,
+            "parallelism": f"one chain per GPU x{world}" if world > 1 else "single GPU",
+            "l2": "inputs 2 GiB > 126 MB L2 (no flush)"}
 
-    c = MOE_CONFIGS[cfg]
-    T, D, F, E, k = c["T"], c["D"], c["F"], c["E"], c["k"]
-    threads = os.cpu_count() or 1
-    oracle.set_threads(threads)
-    rows = sample_rows or 2 * threads
-    x = oracle.to_bf16(oracle.normal("moe_x", (T, D)))
-    wr = oracle.to_bf16(oracle.normal("moe_router", (D, E), sigma=0.02))
-    wg = oracle.to_bf16(oracle.normal("moe_wg", (D, F), sigma=0.02))
-    wu = oracle.to_bf16(oracle.normal("moe_wu", (D, F), sigma=0.02))
-    wd = oracle.to_bf16(oracle.normal("moe_wd", (F, D), sigma=0.02))
-    t0 = time.perf_counter()
-    idx, w = oracle.router_topk(x, wr, k)
-    _, _, perm, inv = oracle.dispatch(idx, E)
-    t_route = time.perf_counter() - t0
-    t0 = time.perf_counter()
-    _, y, _ = oracle.expert_ffn(x[perm[:rows] // k], wg, wu, wd)
-    t_rows = time.perf_counter() - t0
-    ntok = max(1, rows // k)
-    t0 = time.perf_counter()
-    oracle.combine(y[: ntok * k], np.arange(ntok * k, dtype=np.int32).reshape(-1, k), w[:ntok])
-    t_comb = time.perf_counter() - t0
-    total = t_route + t_rows * (T * k) / rows + t_comb * T / ntok
-    return {"value": T / total, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"router+dispatch of all {T} tokens ({t_route:.2f} s), SwiGLU FFN of "
-                      f"{rows} routed rows ({t_rows:.2f} s), combine of {ntok} tokens; "
-                      f"extrapolated to {T * k} rows; oracle/oracle.c, {threads} threads"}
 
-
-# -------------------------------------------------------------------- GEMM
-def bench_gemm(args, world, rank, local):
+def _timed(step, args, world, dev, local):
+    """W warm-up steps, then K steps between barriers and device syncs,
+    CUDA events on the launching stream, SM clocks sampled meanwhile.
+    Returns (this rank's ms per step, clock summary)."""
     import torch
 
     import remora_b200 as rb
 
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    if args.size:
-        batch_local, M, N, K = 1, args.size, args.size, args.size
-        workload = f"dot_general bf16 [{M},{K}]x[{K},{N}] (profiling case)"
-        cfg_key = "gemm_size"
-    elif world == 1:
-        batch_local, M, N, K = 1, 8192, 8192, 8192
-        workload = "dot_general bf16 [8192,8192]x[8192,8192]->[8192,8192], fp32 accumulate"
-        cfg_key = "gemm_8192"
-    else:
-        if 8 % world:
-            raise SystemExit("batched GEMM shards a batch of 8: --gpus must divide 8")
-        batch_local, M, N, K = 8 // world, 4096, 4096, 4096
-        workload = (f"dot_general bf16 batched [8,4096,4096]x[8,4096,4096], batch sharded "
-                    f"{batch_local} per rank over {world} GPUs")
-        cfg_key = "gemm_batched"
-    flop_step = 2.0 * batch_local * M * N * K * world  # the whole job's work per step
-    A = torch.empty(batch_local, M, K, dtype=torch.bfloat16, device=dev)
-    B = torch.empty(batch_local, K, N, dtype=torch.bfloat16, device=dev)
-    C = torch.empty(batch_local, M, N, dtype=torch.bfloat16, device=dev)
-    # each rank fills its own batch slice of the job's seeded tensors
-    rb.fill_uniform(A, rb.stream_key(10 + 100 * rank))
-    rb.fill_uniform(B, rb.stream_key(11 + 100 * rank))
-    a2, b2, c2 = (A[0], B[0], C[0]) if batch_local == 1 else (A, B, C)
-    stream = torch.cuda.current_stream(dev)
-
-    def step():
-        rb.gemm(a2, b2, out=c2)
-
     for _ in range(args.warmup):
         step()
     clk = ClockSampler(local).start()  # NVML set-up before the barrier that aligns the ranks
-    torch.cuda.synchronize(dev)
+    rb.synchronize_and_check(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
+    stream = torch.cuda.current_stream(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with clk:
         ev0.record(stream)
@@ -298,68 +418,8 @@ def bench_gemm(args, world, rank, local):
         torch.cuda.synchronize(dev)
     barrier(world)
     torch.cuda.synchronize(dev)
-    ms_local = ev0.elapsed_time(ev1) / args.steps
-    ms = max_over_ranks(ms_local, world)
-    value = flop_step / (ms * 1e-3) / 1e12
-
-    # end to end through the public API: pinned host inputs in, result out
-    Ah = torch.empty(A.shape, dtype=A.dtype, pin_memory=True)
-    Bh = torch.empty(B.shape, dtype=B.dtype, pin_memory=True)
-    Ch = torch.empty(C.shape, dtype=C.dtype, pin_memory=True)
-    Ah.copy_(A)
-    Bh.copy_(B)
-    e2e_steps = max(3, min(args.steps, 20))
-
-    def e2e_step():
-        A.copy_(Ah, non_blocking=True)
-        B.copy_(Bh, non_blocking=True)
-        rb.gemm(a2, b2, out=c2)
-        Ch.copy_(C, non_blocking=True)
-
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize(dev)
-    barrier(world)
-    ev0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    ev1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / e2e_steps, world)
-    h2d = (A.numel() + B.numel()) * 2 * world
-    d2h = C.numel() * 2 * world
-
-    peaks, src = load_peaks()
-    achieved = 2.0 * batch_local * M * N * K / (ms_local * 1e-3) / 1e12
-    traffic = NCU_TRAFFIC_BYTES.get(cfg_key)
-    line = {
-        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded U(-1,1) bf16)",
-        "config": {"workload": workload, "M": M, "N": N, "K": K, "batch": 8 if world > 1 else 1,
-                   "parallelism": f"batch-sharded x{world}" if world > 1 else "single GPU",
-                   "l2": f"inputs {(A.numel() + B.numel()) * 2 / 2**20:.0f} MiB per GPU "
-                         "> 126 MB L2 (no flush)"},
-        "roofline": {"bound": "tensor", "achieved": achieved,
-                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": achieved / peaks["bf16_tflops"],
-                     "peak_sustained": peaks.get("bf16_tflops_sustained"),
-                     "peak_source": src, "traffic": traffic,
-                     "kernel": "rb::gemm::k_gemm_bf16<true>"},
-        "e2e": {"value": flop_step / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-        "gpu_launches": args.steps,
-        "clocks": clk.summary(),
-    }
-    return line
-
-
-# --------------------------------------------------------------------- MoE
-MOE_CONFIGS = {
-    "4": dict(T=8192, D=4096, F=14336, E=8, k=2),
-    "5": dict(T=65536, D=2048, F=1536, E=64, k=8),
-}
+    rb.synchronize_and_check(dev)
+    return ev0.elapsed_time(ev1) / args.steps, clk.summary()
 
 
 def _cuda_time(fn, reps, dev):
@@ -375,9 +435,169 @@ def _cuda_time(fn, reps, dev):
     return a.elapsed_time(b) / reps
 
 
+def _e2e(step, ins, outs, args, world, dev):
+    """The same step end to end through the public API: every step copies
+    its inputs in from pinned host memory and its result back.  `ins` and
+    `outs` are device tensors; returns (max-over-ranks ms, h2d, d2h bytes
+    for the whole job)."""
+    import torch
+
+    hin = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in ins]
+    hout = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in outs]
+    for h, t in zip(hin, ins):
+        h.copy_(t)
+
+    def e2e_step():
+        for h, t in zip(hin, ins):
+            t.copy_(h, non_blocking=True)
+        step()
+        for h, t in zip(hout, outs):
+            h.copy_(t, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(_cuda_time(e2e_step, max(3, min(args.steps, 10)), dev), world)
+    h2d = sum(t.numel() * t.element_size() for t in ins) * world
+    d2h = sum(t.numel() * t.element_size() for t in outs) * world
+    return ms, h2d, d2h
+
+
+def _line(args, world, value, unit, ms, scaling, dtype, data, roofline, e2e, launches, clocks,
+          detail):
+    return {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": dtype,
+            "data": data, "config": workload_config(args, world), "roofline": roofline,
+            "e2e": e2e, "gpu_launches": launches, "clocks": clocks, "detail": detail}
+
+
+def _tensor_roofline(achieved, peaks, src, kernel, traffic=None, **extra):
+    return {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
+            "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+            "peak_sustained": peaks.get("bf16_tflops_sustained"), "peak_source": src,
+            "traffic": traffic, "kernel": kernel, **extra}
+
+
+def _moe_tensors(rb, c, dev, rank, world, sliced):
+    """x [T, D] and the expert weights from the seeded generator; with
+    `sliced`, this rank's T/world tokens and E/world experts."""
+    import torch
+
+    T, D, F, E = c["T"], c["D"], c["F"], c["E"]
+    x = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    wr = torch.empty(D, E, dtype=torch.bfloat16, device=dev)
+    rb.fill_normal(x, rb.stream_key(30), 0.0, 1.0)
+    rb.fill_normal(wr, rb.stream_key(31), 0.0, 0.02)
+    if sliced:
+        tl = T // world
+        x = x[rank * tl:(rank + 1) * tl].contiguous()
+    ws = []
+    Epr = E // world if sliced else E
+    for sid, shape in ((32, (E, D, F)), (33, (E, D, F)), (34, (E, F, D))):
+        full = torch.empty(shape, dtype=torch.bfloat16, device=dev)
+        rb.fill_normal(full, rb.stream_key(sid), 0.0, 0.02)
+        ws.append(full[rank * Epr:(rank + 1) * Epr].contiguous() if sliced else full)
+        del full
+    torch.cuda.synchronize(dev)
+    return x, wr, ws
+
+
+def bench_moe_ep(args, world, rank, local):
+    """The 65536-token, 64-expert MoE layer: one GPU runs it whole; N > 1
+    GPUs split tokens and experts and exchange rows over NVLink."""
+    import torch
+
+    import remora_b200 as rb
+
+    c = MOE_CONFIGS["5"]
+    T, D, F, E, k = c["T"], c["D"], c["F"], c["E"], c["k"]
+    if T % world or E % world:
+        raise SystemExit(f"the layer does not split over {world} ranks")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    tl = T // world
+    x, wr, (wg, wu, wd) = _moe_tensors(rb, c, dev, rank, world, sliced=world > 1)
+    out = torch.empty(tl, D, dtype=torch.bfloat16, device=dev)
+    peaks, src = load_peaks()
+    pep = None
+    if world == 1:
+        ws = torch.empty(rb.moe_workspace_bytes(T, D, F, E, k), dtype=torch.uint8, device=dev)
+
+        def step():
+            rb.moe_layer(x, wr, wg, wu, wd, k, out=out, workspace=ws)
+    elif args.ep_mode == "nccl":
+        from remora_b200.ep_nccl import NcclEP
+
+        pep = NcclEP(tl, D, F, E, k, device=dev)
+
+        def step():
+            pep.forward(x, wr, wg, wu, wd, out=out)
+    else:
+        from remora_b200.ep_p2p import PeerEP
+
+        pep = PeerEP(tl, D, F, E, k, device=dev, fused=args.ep_mode == "p2p")
+
+        def step():
+            pep.forward(x, wr, wg, wu, wd, out=out)
+
+    ms_local, clocks = _timed(step, args, world, dev, local)
+    rank_ms = all_ranks(ms_local, world)
+    ms = max(rank_ms)
+    e2e_ms, h2d, d2h = _e2e(step, [x], [out], args, world, dev)
+
+    # dominant kernel, timed by itself with CUDA events after the timed region
+    if world == 1:
+        idx, w = rb.moe_router_topk(x, wr, k)
+        counts, offsets, perm, inv = rb.moe_dispatch(idx, E)
+        xs = rb.moe_gather(x, perm, k)
+        h = rb.grouped_gemm_swiglu(xs, wg, wu, offsets)
+        y = rb.grouped_gemm(h, wd, offsets)
+        t_up = _cuda_time(lambda: rb.grouped_gemm_swiglu(xs, wg, wu, offsets, out=h), 5, dev)
+        t_down = _cuda_time(lambda: rb.grouped_gemm(h, wd, offsets, out=y), 5, dev)
+        t_router = _cuda_time(lambda: rb.moe_router_topk(x, wr, k, idx=idx, w=w), 5, dev)
+        rows = T * k
+        up_tf = 4.0 * rows * D * F / (t_up * 1e-3) / 1e12
+        roof = _tensor_roofline(up_tf, peaks, src, "rb::moe::k_grouped_gemm<true> (SwiGLU)",
+                                NCU_TRAFFIC_BYTES.get("moe_swiglu_5"),
+                                kernel_ms=t_up,
+                                down_tflops=2.0 * rows * F * D / (t_down * 1e-3) / 1e12)
+        detail = {"kernel_ms": {"grouped_swiglu": t_up, "grouped_down": t_down,
+                                "router_topk": t_router},
+                  "expert_tflops_layer": 6.0 * D * F * rows / (ms * 1e-3) / 1e12}
+        launches = 8
+    else:
+        pep.profile = True
+        phases = []
+        for _ in range(5):
+            step()
+            phases.append(dict(pep.phase_ms))
+        pep.profile = False
+        rows_here = pep.rows_received()
+        ph = {n: statistics.median(p[n] for p in phases) for n in phases[0]}
+        t_exp = ph["experts"]
+        exp_tf = 6.0 * D * F * rows_here / (t_exp * 1e-3) / 1e12
+        roof = _tensor_roofline(exp_tf, peaks, src, pep.dominant_kernel,
+                                NCU_TRAFFIC_BYTES.get("moe_ep_experts"), kernel_ms=t_exp,
+                                rows=rows_here)
+        detail = {"rank_ms": [round(v, 4) for v in rank_ms],
+                  "phase_ms_rank0": {n: round(v, 4) for n, v in ph.items()},
+                  "expert_tflops_per_gpu_layer": 6.0 * D * F * T * k / world / (ms * 1e-3) / 1e12}
+        launches = pep.launches_per_layer
+    line = _line(args, world, T / (ms * 1e-3), "tokens/s", ms, "strong", "bf16",
+                 "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, bf16)", roof,
+                 {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                  "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                 launches * args.steps, clocks, detail)
+    if pep is not None:
+        pep.close()
+    return line
+
+
 def bench_moe(args, world, rank, local):
-    """The MoE layer (router, dispatch, SwiGLU expert GEMMs, combine) on one
-    GPU per rank; tokens/s = T / layer time."""
+    """One whole MoE layer per GPU (config 4 or 5); tokens/s = T / layer time
+    (summed over the ranks' independent layers)."""
     import torch
 
     import remora_b200 as rb
@@ -386,203 +606,82 @@ def bench_moe(args, world, rank, local):
     T, D, F, E, k = c["T"], c["D"], c["F"], c["E"], c["k"]
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    x = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
-    wr = torch.empty(D, E, dtype=torch.bfloat16, device=dev)
-    wg = torch.empty(E, D, F, dtype=torch.bfloat16, device=dev)
-    wu = torch.empty(E, D, F, dtype=torch.bfloat16, device=dev)
-    wd = torch.empty(E, F, D, dtype=torch.bfloat16, device=dev)
-    for t, stream_id, sig in ((x, 30, 1.0), (wr, 31, 0.02), (wg, 32, 0.02), (wu, 33, 0.02),
-                              (wd, 34, 0.02)):
-        rb.fill_normal(t, rb.stream_key(stream_id + 100 * rank), 0.0, sig)
+    x, wr, (wg, wu, wd) = _moe_tensors(rb, c, dev, rank, world, sliced=False)
     out = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
     ws = torch.empty(rb.moe_workspace_bytes(T, D, F, E, k), dtype=torch.uint8, device=dev)
 
     def step():
         rb.moe_layer(x, wr, wg, wu, wd, k, out=out, workspace=ws)
 
-    for _ in range(args.warmup):
-        step()
-    clk = ClockSampler(local).start()  # NVML set-up before the barrier that aligns the ranks
-    rb.synchronize_and_check(dev)
-    barrier(world)
-    stream = torch.cuda.current_stream(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step()
-        ev1.record(stream)
-        torch.cuda.synchronize(dev)
-    barrier(world)
-    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
-    rb.synchronize_and_check(dev)
-
-    # per-kernel times of the expert GEMMs on the same routing (roofline)
+    ms_local, clocks = _timed(step, args, world, dev, local)
+    ms = max_over_ranks(ms_local, world)
+    e2e_ms, h2d, d2h = _e2e(step, [x], [out], args, world, dev)
     idx, w = rb.moe_router_topk(x, wr, k)
     counts, offsets, perm, inv = rb.moe_dispatch(idx, E)
     xs = rb.moe_gather(x, perm, k)
     h = rb.grouped_gemm_swiglu(xs, wg, wu, offsets)
     y = rb.grouped_gemm(h, wd, offsets)
-    reps = 5
-    t_up = _cuda_time(lambda: rb.grouped_gemm_swiglu(xs, wg, wu, offsets, out=h), reps, dev)
-    t_down = _cuda_time(lambda: rb.grouped_gemm(h, wd, offsets, out=y), reps, dev)
-    t_router = _cuda_time(lambda: rb.moe_router_topk(x, wr, k, idx=idx, w=w), reps, dev)
+    t_up = _cuda_time(lambda: rb.grouped_gemm_swiglu(xs, wg, wu, offsets, out=h), 5, dev)
+    t_down = _cuda_time(lambda: rb.grouped_gemm(h, wd, offsets, out=y), 5, dev)
+    t_router = _cuda_time(lambda: rb.moe_router_topk(x, wr, k, idx=idx, w=w), 5, dev)
     rows = T * k
-    flop_up = 2.0 * rows * D * F * 2
-    flop_down = 2.0 * rows * F * D
     peaks, src = load_peaks()
-    up_tf = flop_up / (t_up * 1e-3) / 1e12
-
-    # end to end: tokens in from pinned host memory, layer output back
-    xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
-    oh = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-    xh.copy_(x)
-
-    def e2e_step():
-        x.copy_(xh, non_blocking=True)
-        step()
-        oh.copy_(out, non_blocking=True)
-
-    for _ in range(2):
-        e2e_step()
-    e2e_ms = max_over_ranks(_cuda_time(e2e_step, max(3, min(args.steps, 10)), dev), world)
+    up_tf = 4.0 * rows * D * F / (t_up * 1e-3) / 1e12
+    roof = _tensor_roofline(up_tf, peaks, src, "rb::moe::k_grouped_gemm<true> (SwiGLU)",
+                            NCU_TRAFFIC_BYTES.get("moe_swiglu_" + args.moe_config),
+                            kernel_ms=t_up,
+                            down_tflops=2.0 * rows * F * D / (t_down * 1e-3) / 1e12)
     tokens = T * world
-    return {
-        "metric": METRIC, "value": tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, bf16)",
-        "config": {"workload": f"MoE layer config {args.moe_config}: T={T} D={D} F={F} E={E} "
-                               f"top-{k}, SwiGLU experts", "parallelism":
-                   f"independent layer per rank x{world}" if world > 1 else "single GPU",
-                   "expert_flop_per_step": (flop_up + flop_down) * world,
-                   "expert_tflops": (flop_up + flop_down) / (ms * 1e-3) / 1e12,
-                   "kernel_ms": {"grouped_swiglu": t_up, "grouped_down": t_down,
-                                 "router_topk": t_router},
-                   "l2": "weights and activations > 126 MB L2 (no flush)"},
-        "roofline": {"bound": "tensor", "achieved": up_tf, "peak": peaks["bf16_tflops"],
-                     "unit": "TFLOP/s", "frac": up_tf / peaks["bf16_tflops"],
-                     "peak_sustained": peaks.get("bf16_tflops_sustained"), "peak_source": src,
-                     "traffic": NCU_TRAFFIC_BYTES.get("moe_swiglu_" + args.moe_config),
-                     "kernel": "rb::moe::k_grouped_gemm<true>",
-                     "down_tflops": flop_down / (t_down * 1e-3) / 1e12},
-        "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": x.numel() * 2 * world,
-                "d2h_bytes_per_step": out.numel() * 2 * world, "ms_per_step": e2e_ms},
-        "gpu_launches": 8 * args.steps, "clocks": clk.summary(),
-    }
+    return _line(args, world, tokens / (ms * 1e-3), "tokens/s", ms, "weak", "bf16",
+                 "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, bf16)", roof,
+                 {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                 8 * args.steps, clocks,
+                 {"kernel_ms": {"grouped_swiglu": t_up, "grouped_down": t_down,
+                                "router_topk": t_router},
+                  "expert_tflops_layer": 6.0 * D * F * rows / (ms * 1e-3) / 1e12})
 
 
-def bench_moe_ep(args, world, rank, local):
-    """Expert-parallel MoE, config 5: 65536 tokens split over the ranks,
-    64 experts split over the ranks (8 per GPU at 8 GPUs), token dispatch
-    and combine by NCCL all-to-all.  One GPU runs the single-GPU layer."""
+def bench_gemm(args, world, rank, local):
     import torch
 
     import remora_b200 as rb
-    from remora_b200.ep import moe_ep_forward
 
-    c = MOE_CONFIGS["5"]
-    T, D, F, E, k = c["T"], c["D"], c["F"], c["E"], c["k"]
-    if T % world or E % world:
-        raise SystemExit(f"config 5 does not split over {world} ranks")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    tl, Epr = T // world, E // world
-    x = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
-    wr = torch.empty(D, E, dtype=torch.bfloat16, device=dev)
-    rb.fill_normal(x, rb.stream_key(30), 0.0, 1.0)
-    rb.fill_normal(wr, rb.stream_key(31), 0.0, 0.02)
-    x = x[rank * tl:(rank + 1) * tl].contiguous()
-    ws = []
-    for sid, shape in ((32, (E, D, F)), (33, (E, D, F)), (34, (E, F, D))):
-        full = torch.empty(shape, dtype=torch.bfloat16, device=dev)
-        rb.fill_normal(full, rb.stream_key(sid), 0.0, 0.02)
-        ws.append(full if world == 1 else full[rank * Epr:(rank + 1) * Epr].contiguous())
-        del full
-    wg, wu, wd = ws
-    out = torch.empty(tl, D, dtype=torch.bfloat16, device=dev)
-    lws = (torch.empty(rb.moe_workspace_bytes(T, D, F, E, k), dtype=torch.uint8, device=dev)
-           if world == 1 else None)
-
-    pep = None
-    if world > 1 and args.ep_mode in ("p2p", "p2p-split"):
-        from remora_b200.ep_p2p import PeerEP
-
-        pep = PeerEP(tl, D, F, E, k, device=dev, fused=args.ep_mode == "p2p")
+    cfg = workload_config(args, world)
+    if args.size or world == 1:
+        batch_local, M, N, K = 1, cfg["M"], cfg["N"], cfg["K"]
+        key = "gemm_size" if args.size else "gemm_8192"
+    else:
+        if 8 % world:
+            raise SystemExit("batched GEMM shards a batch of 8: --gpus must divide 8")
+        batch_local, M, N, K = 8 // world, 4096, 4096, 4096
+        key = "gemm_batched"
+    A = torch.empty(batch_local, M, K, dtype=torch.bfloat16, device=dev)
+    B = torch.empty(batch_local, K, N, dtype=torch.bfloat16, device=dev)
+    C = torch.empty(batch_local, M, N, dtype=torch.bfloat16, device=dev)
+    # each rank fills its own batch slice of the job's seeded tensors
+    rb.fill_uniform(A, rb.stream_key(10 + 100 * rank))
+    rb.fill_uniform(B, rb.stream_key(11 + 100 * rank))
+    a2, b2, c2 = (A[0], B[0], C[0]) if batch_local == 1 else (A, B, C)
 
     def step():
-        if world == 1:
-            rb.moe_layer(x, wr, wg, wu, wd, k, out=out, workspace=lws)
-        elif pep is not None:
-            pep.forward(x, wr, wg, wu, wd, out=out)
-        else:
-            out.copy_(moe_ep_forward(x, wr, wg, wu, wd, k, E, chunks=args.ep_chunks or None))
+        rb.gemm(a2, b2, out=c2)
 
-    for _ in range(args.warmup):
-        step()
-    clk = ClockSampler(local).start()  # NVML set-up before the barrier that aligns the ranks
-    rb.synchronize_and_check(dev)
-    barrier(world)
-    torch.cuda.synchronize(dev)
-    stream = torch.cuda.current_stream(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step()
-        ev1.record(stream)
-        torch.cuda.synchronize(dev)
-    barrier(world)
-    ms_local = ev0.elapsed_time(ev1) / args.steps
-    rank_ms = all_ranks(ms_local, world)
-    ms = max(rank_ms)
-    xh = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
-    oh = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-    xh.copy_(x)
-
-    def e2e_step():
-        x.copy_(xh, non_blocking=True)
-        step()
-        oh.copy_(out, non_blocking=True)
-
-    e2e_step()
-    barrier(world)
-    e2e_ms = max_over_ranks(_cuda_time(e2e_step, max(3, min(args.steps, 10)), dev), world)
-    flop = 6.0 * D * F * T * k
+    ms_local, clocks = _timed(step, args, world, dev, local)
+    ms = max_over_ranks(ms_local, world)
+    e2e_ms, h2d, d2h = _e2e(step, [A, B], [C], args, world, dev)
+    flop_local = 2.0 * batch_local * M * N * K
     peaks, src = load_peaks()
-    per_gpu_tf = flop / world / (ms * 1e-3) / 1e12
-    return {
-        "metric": METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights, bf16)",
-        "config": {"workload": f"expert-parallel MoE config 5: T={T} D={D} F={F} E={E} top-{k}, "
-                               f"{Epr} experts and {tl} tokens per GPU",
-                   "parallelism": (f"EP{world} ({EP_MODES[args.ep_mode]})"
-                                   if world > 1 else "single GPU"),
-                   "ep_chunks": args.ep_chunks or "default",
-                   "expert_flop_per_step": flop,
-                   "rank_ms": [round(v, 4) for v in rank_ms]},
-        "roofline": {"bound": "tensor", "achieved": per_gpu_tf, "peak": peaks["bf16_tflops"],
-                     "unit": "TFLOP/s", "frac": per_gpu_tf / peaks["bf16_tflops"],
-                     "peak_source": src, "traffic": None,
-                     "kernel": "whole layer per GPU (expert FLOP / layer time)"},
-        "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": x.numel() * 2 * world,
-                "d2h_bytes_per_step": out.numel() * 2 * world, "ms_per_step": e2e_ms},
-        "gpu_launches": (EP_LAUNCHES[args.ep_mode] if world > 1 else 8) * args.steps,
-        "clocks": clk.summary(),
-    }
-
-
-# kernels of one EP layer: router 1, dispatch 3, then (fused) meta, experts (copy + SwiGLU +
-# down), barrier, combine; (split) scatter, barrier, segments, SwiGLU, down, barrier, combine
-EP_LAUNCHES = {"p2p": 8, "p2p-split": 11, "nccl": 9}
-EP_MODES = {"p2p": "NVLink peer memory: row copy, SwiGLU and down tiles in one cooperative "
-                   "kernel, down epilogues store to the source ranks",
-            "p2p-split": "NVLink peer memory: scatter kernel, barrier, GEMMs",
-            "nccl": "NCCL all-to-all"}
+    achieved = flop_local / (ms_local * 1e-3) / 1e12
+    roof = _tensor_roofline(achieved, peaks, src, "rb::gemm::k_gemm_bf16",
+                            NCU_TRAFFIC_BYTES.get(key), kernel_ms=ms_local)
+    return _line(args, world, flop_local * world / (ms * 1e-3) / 1e12, "TFLOP/s", ms,
+                 "strong", "bf16", "synthetic (seeded U(-1,1) bf16)", roof,
+                 {"value": flop_local * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                 args.steps, clocks, {})
 
 
 def bench_attention(args, world, rank, local):
@@ -606,61 +705,24 @@ def bench_attention(args, world, rank, local):
     def step():
         rb.attention(q, k, v, causal=True, out=o)
 
-    for _ in range(args.warmup):
-        step()
-    clk = ClockSampler(local).start()  # NVML set-up before the barrier that aligns the ranks
-    torch.cuda.synchronize(dev)
-    barrier(world)
-    stream = torch.cuda.current_stream(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step()
-        ev1.record(stream)
-        torch.cuda.synchronize(dev)
-    barrier(world)
-    ms_local = ev0.elapsed_time(ev1) / args.steps
+    ms_local, clocks = _timed(step, args, world, dev, local)
     ms = max_over_ranks(ms_local, world)
+    e2e_ms, h2d, d2h = _e2e(step, [q, k, v], [o], args, world, dev)
     flop = 4.0 * B * H * S * S * Dh / 2.0
-    qh, kh, vh, oh = (torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (q, k, v, o))
-    qh.copy_(q), kh.copy_(k), vh.copy_(v)
-
-    def e2e_step():
-        q.copy_(qh, non_blocking=True)
-        k.copy_(kh, non_blocking=True)
-        v.copy_(vh, non_blocking=True)
-        step()
-        oh.copy_(o, non_blocking=True)
-
-    e2e_step()
-    barrier(world)
-    e2e_ms = max_over_ranks(_cuda_time(e2e_step, max(3, min(args.steps, 10)), dev), world)
     peaks, src = load_peaks()
     achieved = flop / world / (ms_local * 1e-3) / 1e12
-    return {
-        "metric": METRIC, "value": flop / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) bf16)",
-        "config": {"workload": f"causal attention bf16 [{B},{H},{S},{Dh}], {bh} (batch, head) "
-                               f"pairs per GPU", "flop_convention": "4*B*H*S^2*Dh/2 (causal half)",
-                   "parallelism": f"batch x heads sharded x{world}" if world > 1 else "single GPU",
-                   "l2": "q, k, v 402 MB > 126 MB L2 (no flush)"},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"],
-                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
-                     "peak_source": src, "traffic": None, "kernel": "rb::attn::k_attention_fwd"},
-        "e2e": {"value": flop / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": 3 * q.numel() * 2 * world,
-                "d2h_bytes_per_step": o.numel() * 2 * world, "ms_per_step": e2e_ms},
-        "gpu_launches": args.steps, "clocks": clk.summary(),
-    }
+    roof = _tensor_roofline(achieved, peaks, src, "rb::attn::k_attention_fwd",
+                            NCU_TRAFFIC_BYTES.get("attention"), kernel_ms=ms_local)
+    return _line(args, world, flop / (ms * 1e-3) / 1e12, "TFLOP/s", ms, "strong", "bf16",
+                 "synthetic (seeded N(0,1) bf16)", roof,
+                 {"value": flop / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                 args.steps, clocks, {})
 
 
-# ------------------------------------------------------------- elementwise
 def bench_elementwise(args, world, rank, local):
-    """scale -> add -> exp chain: the named [1,8,128,128] shape (latency
-    bound, L2 resident) and a 2^28-element sweep where HBM BW is judged."""
+    """scale -> add -> exp chain over 2^28 f32 elements (HBM bound), with the
+    named [1,8,128,128] shape's time per call (latency bound) beside it."""
     import torch
 
     import remora_b200 as rb
@@ -671,121 +733,115 @@ def bench_elementwise(args, world, rank, local):
     s = torch.empty(n, device=dev)
     b = torch.empty(n, device=dev)
     o = torch.empty(n, device=dev)
-    rb.fill_normal(s, rb.stream_key(1))
-    rb.fill_normal(b, rb.stream_key(2))
-    stream = torch.cuda.current_stream(dev)
-    for _ in range(args.warmup):
+    rb.fill_normal(s, rb.stream_key(1 + 100 * rank))
+    rb.fill_normal(b, rb.stream_key(2 + 100 * rank))
+
+    def step():
         rb.scale_add_exp(s, b, 0.125, out=o)
-    clk = ClockSampler(local).start()  # NVML set-up before the barrier that aligns the ranks
-    torch.cuda.synchronize(dev)
-    barrier(world)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            rb.scale_add_exp(s, b, 0.125, out=o)
-        ev1.record(stream)
-        torch.cuda.synchronize(dev)
-    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+
+    ms_local, clocks = _timed(step, args, world, dev, local)
+    ms = max_over_ranks(ms_local, world)
+    e2e_ms, h2d, d2h = _e2e(step, [s, b], [o], args, world, dev)
     bytes_step = 12.0 * n * world
-    gbs = bytes_step / (ms * 1e-3) / 1e9
     small = rb.run_test("elementwise_chain", device=local, iters=200, warmup=20)
     peaks, src = load_peaks()
-    return {
-        "metric": METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) f32)",
-        "config": {"workload": "exp(s*0.125+b) f32, 2^28 elements (3 GiB per step)",
-                   "named_shape_us_per_call": small["ms_per_iter"] * 1e3,
-                   "l2": "inputs 2 GiB > 126 MB L2"},
-        "roofline": {"bound": "hbm", "achieved": gbs / world, "peak": peaks["hbm_gbs"],
-                     "unit": "GB/s", "frac": gbs / world / peaks["hbm_gbs"],
-                     "peak_source": src, "traffic": NCU_TRAFFIC_BYTES.get("elementwise")},
-        "gpu_launches": args.steps, "clocks": clk.summary(),
-    }
+    gbs_local = 12.0 * n / (ms_local * 1e-3) / 1e9
+    roof = {"bound": "hbm", "achieved": gbs_local, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+            "frac": gbs_local / peaks["hbm_gbs"], "peak_source": src,
+            "traffic": NCU_TRAFFIC_BYTES.get("elementwise"), "kernel": "rb::ew::k_scale_add_exp_v4",
+            "kernel_ms": ms_local}
+    return _line(args, world, bytes_step / (ms * 1e-3) / 1e9, "GB/s", ms, "weak", "f32",
+                 "synthetic (seeded N(0,1) f32)", roof,
+                 {"value": bytes_step / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                  "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                 args.steps, clocks, {"named_shape_us_per_call": small["ms_per_iter"] * 1e3})
+
+
+# kernels of one layer: single GPU: router 1, dispatch 3, gather, SwiGLU, down, combine;
+# expert-parallel over peer memory: router 1, dispatch 3, then (fused) meta, experts
+# (copy + SwiGLU + down), barrier, combine; (split) scatter, barrier, segments, SwiGLU,
+# down, barrier, combine
+EP_MODES = {"p2p": "token exchange over NVLink peer memory inside the expert kernel",
+            "p2p-split": "token exchange over NVLink peer memory (scatter kernel, barrier, "
+                         "grouped GEMMs)",
+            "nccl": "token exchange by NCCL all-to-all-v through the library's C ABI"}
 
 
 # --------------------------------------------------------- reference arm
 def reference_arm(args, world, rank):
-    """The reference's CPU path (its loop nest, restated in oracle/) on all
-    host threads, on a bounded row sample of the same GEMM per step."""
+    """The reference's CPU path (its loop nests, restated in oracle/) on all
+    host threads, one bounded sample of the same workload per step; rank 0
+    only."""
     if rank != 0:
         return None
-    import oracle
-
     threads = os.cpu_count() or 1
-    # calibrate: rows per step so that the whole run stays within ~2 minutes
-    rate, rows, el = cpu_gemm_rows_rate(threads, 2.0, threads)
-    sec_per_row = el / rows
-    per_step = max(1, int(min(threads * 4, 100.0 / (args.steps + args.warmup) / sec_per_row)))
-    for _ in range(args.warmup):
-        cpu_gemm_rows_rate(per_step, 0.0, threads)
+    run, what = cpu_sampler(args.workload, threads, args.moe_config)
+    chunk = _chunk(args.workload, threads)
     t0 = time.perf_counter()
+    run(chunk)  # calibration call
+    per_call = max(time.perf_counter() - t0, 1e-6)
+    calls = max(1, int(90.0 / (args.steps + args.warmup) / per_call))
+    for _ in range(args.warmup):
+        for _ in range(calls):
+            run(chunk)
+    done, t0 = 0.0, time.perf_counter()
     for _ in range(args.steps):
-        cpu_gemm_rows_rate(per_step, 0.0, threads)
+        for _ in range(calls):
+            done += run(chunk)
     el = time.perf_counter() - t0
-    v = 2.0 * per_step * 8192 * 8192 * args.steps / el / 1e12
-    sample = (f"{per_step} output rows of the 8192^3 bf16 GEMM per step "
-              f"(oracle/oracle.c loop nest, {threads} threads)")
+    unit, scale = CPU_UNITS[args.workload]
+    v = done / el / scale
+    sample = f"{calls * chunk} {what} per step on {threads} threads (gcc -O2 -fopenmp)"
     return {
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": el / args.steps * 1e3, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded U(-1,1) bf16)",
-        "config": {"workload": "dot_general bf16 [8192,8192]x[8192,8192]->[8192,8192], fp32 "
-                               "accumulate (row sample per step)"},
-        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+        "impl": "reference", "metric": METRIC, "value": v, "unit": unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": el / args.steps * 1e3,
+        "higher_is_better": True,
+        "scaling": {"moe_ep": "strong", "gemm": "strong", "attention": "strong"}.get(
+            args.workload, "weak"),
+        "vs_baseline": None, "dtype": "f32" if args.workload == "elementwise" else "bf16",
+        "data": "synthetic (seeded inputs, the GPU arm's generator)",
+        "config": workload_config(args, world),
+        "cpu_baseline": {"value": v, "unit": unit, "cores": threads, "kind": "port",
                          "sample": sample},
-        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "e2e": {"value": v, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["gemm", "elementwise", "moe", "moe_ep", "attention"],
-                    default="gemm")
-    ap.add_argument("--moe-config", choices=sorted(MOE_CONFIGS), default="4")
-    ap.add_argument("--ep-mode", choices=["p2p", "p2p-split", "nccl"], default="p2p",
-                    help="moe_ep: token exchange by the library's peer-memory kernels or NCCL")
-    ap.add_argument("--ep-chunks", type=int, default=0,
-                    help="moe_ep: token pieces per layer for comm/compute overlap (0 = default)")
+    ap.add_argument("--workload", choices=["moe_ep", "moe", "gemm", "attention", "elementwise"],
+                    default="moe_ep")
+    ap.add_argument("--moe-config", choices=sorted(MOE_CONFIGS), default="4",
+                    help="moe: which layer each GPU runs")
+    ap.add_argument("--ep-mode", choices=sorted(EP_MODES), default="p2p",
+                    help="moe_ep at N > 1: how the token exchange runs")
     ap.add_argument("--size", type=int, default=0,
                     help="gemm: run an MxNxK = size^3 case instead of the configuration")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    world, rank, local = dist_setup(args)
     if args.impl == "reference":
-        line = reference_arm(args, world, rank)
+        # no process group: rank 0 alone runs the CPU path, the other ranks exit
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        line = reference_arm(args, world, int(os.environ.get("RANK", "0")))
         if line is not None:
             print(json.dumps(line), flush=True)
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.destroy_process_group()
         return
+    world, rank, local = dist_setup(args)
     from remora_b200 import build
 
     build.build()  # no-op when the in-tree library is current
     fn = {"gemm": bench_gemm, "elementwise": bench_elementwise, "moe": bench_moe,
           "moe_ep": bench_moe_ep, "attention": bench_attention}[args.workload]
     line = fn(args, world, rank, local)
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        if args.workload == "gemm":
-            line["cpu_baseline"] = cpu_baseline_gemm()
-        elif args.workload == "moe":
-            line["cpu_baseline"] = cpu_baseline_moe(args.moe_config)
-        else:
-            line["cpu_baseline"] = None
-    elif rank == 0:
-        line["cpu_baseline"] = None
     if rank == 0:
+        line["cpu_baseline"] = (cpu_baseline(args.workload, args.moe_config)
+                                if world == 1 and not args.no_cpu_baseline else None)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
