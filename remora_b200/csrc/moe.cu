@@ -20,7 +20,6 @@ namespace moe {
 // loop nest (linalg.fill + reduction, convert-linalg-to-loops), so the
 // top-k indices are bit-identical to it.  A bf16 x bf16 product is exact in
 // fp32, so fmaf(a, b, acc) == acc + a*b here.
-constexpr int kRouterThreads = 256;
 constexpr int kRouterDCh = 32;             // d per shared-memory chunk
 constexpr int kRowPadF = kRouterDCh + 4;   // padded f32 row (16-byte aligned rows)
 
@@ -43,15 +42,18 @@ __device__ __forceinline__ bool topk_before(float a, int ia, float b, int ib) {
 // router chunks are converted to f32 once while staging; the next chunk's
 // global loads are issued into registers before the current chunk is used.
 // Top-k: per token, a segmented butterfly over the LE lanes of its group.
-// Host contract: RT <= LE (at most 256 tokens per block), E % 8 == 0 or
-// E <= 128, k <= 16.
-template <int RT, int EPL>
-__global__ void __launch_bounds__(kRouterThreads)
+// WARPS warps per block: fewer warps per block give more blocks (every SM
+// busy) when there are few tokens and the register block RT x EPL is large.
+// Host contract: RT <= LE (so at most WARPS * 32 tokens per block),
+// E % 8 == 0 or E <= 128, k <= 16.
+template <int RT, int EPL, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
     k_router_topk(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr, int T, int D,
                   int E, int k, int LE, int32_t* __restrict__ idx_out,
                   float* __restrict__ w_out) {
   extern __shared__ __align__(16) uint8_t sm_raw[];
-  constexpr int kWarps = kRouterThreads / 32;
+  constexpr int kRouterThreads = WARPS * 32;
+  constexpr int kWarps = WARPS;
   constexpr int kDC8 = kRouterDCh / 8;
   const int LT = 32 / LE;              // token groups per warp
   const int TGB = kWarps * LT;         // token groups per block
@@ -79,11 +81,12 @@ __global__ void __launch_bounds__(kRouterThreads)
   const bool vec_w = (E % 8) == 0;
   const int nx = TPB * kDC8;                              // x pieces of 8 per chunk
   const int nw = vec_w ? kRouterDCh * (E / 8) : kRouterDCh * E;
-  constexpr int kXPT = 256 * kDC8 / kRouterThreads;       // TPB <= 256
-  constexpr int kWPT = 4;                                 // 16-byte pieces (E <= 256)
-  constexpr int kWPS = 16;                                // single values (E <= 128)
+  // pieces per thread: TPB <= WARPS*32 (RT <= LE) and E <= 32*EPL (LE <= 32)
+  constexpr int kXPT = kDC8;
+  constexpr int kWPT = (128 * EPL + kRouterThreads - 1) / kRouterThreads;   // 16-byte pieces
+  constexpr int kWPS = (1024 * EPL + kRouterThreads - 1) / kRouterThreads;  // single values
   uint4 xpre[kXPT];
-  uint32_t wreg[4 * kWPT];
+  uint32_t wreg[4 * kWPT > kWPS ? 4 * kWPT : kWPS];
   auto load_chunk = [&](int d0) {
     const int dc = min(kRouterDCh, D - d0);
 #pragma unroll
@@ -251,28 +254,89 @@ __global__ void __launch_bounds__(kDispThreads)
     block_counts[(int64_t)blockIdx.x * E + i] = cnt[i];
 }
 
-// Per-expert exclusive scan over blocks, then the expert offsets.
-__global__ void k_dispatch_scan(int32_t* __restrict__ block_counts, int nblocks, int E,
-                                int32_t* __restrict__ counts, int32_t* __restrict__ offsets) {
-  extern __shared__ int tot[];  // [E]
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int run = 0;
-    for (int b = 0; b < nblocks; ++b) {
-      const int c = block_counts[(int64_t)b * E + e];
-      block_counts[(int64_t)b * E + e] = run;  // becomes the block's base within e
-      run += c;
+// Per-expert exclusive scan over the dispatch blocks, then the expert
+// offsets.  Lanes run over experts (a warp reads 32 consecutive counts of
+// one block row: coalesced) and the blocks are split into W contiguous
+// parts, one warp each, for the 32 experts of its group: each warp sums its
+// part, the part sums are scanned in shared memory, and each warp rewrites
+// its part in place as the blocks' bases within each expert.  (One thread
+// per expert walking the blocks with dependent loads took 121 us at 512
+// blocks x 64 experts; one warp per expert reading a column, 42 us, bound
+// by uncoalesced L1 wavefronts.)
+constexpr int kScanThreads = 1024;
+
+__global__ void __launch_bounds__(kScanThreads)
+    k_dispatch_scan(int32_t* __restrict__ block_counts, int nblocks, int E,
+                    int32_t* __restrict__ counts, int32_t* __restrict__ offsets) {
+  __shared__ int part_sum[32][33], part_base[32][33];
+  __shared__ int tot[256];  // E <= 256 (the dispatch entry points reject more)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = (E + 31) / 32;          // expert groups of 32 lanes (E <= 256: G <= 8)
+  const int W = 32 / G;                 // warps (block parts) per group
+  const int g = warp / W, part = warp % W;
+  const int e = g * 32 + lane;
+  const bool act = g < G && e < E;
+  const int per = (nblocks + W - 1) / W;
+  const int b_lo = min(nblocks, part * per), b_hi = min(nblocks, b_lo + per);
+  int sum = 0;
+  if (act) {
+    int b = b_lo;
+    for (; b + 8 <= b_hi; b += 8) {
+      int v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = block_counts[(int64_t)(b + j) * E + e];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum += v[j];
     }
-    tot[e] = run;
-    counts[e] = run;
+    for (; b < b_hi; ++b) sum += block_counts[(int64_t)b * E + e];
+  }
+  if (g < G) part_sum[warp][lane] = sum;
+  __syncthreads();
+  if (g < G && part == 0) {
+    int run = 0;
+    for (int p = 0; p < W; ++p) {
+      part_base[g * W + p][lane] = run;
+      run += part_sum[g * W + p][lane];
+    }
+    if (act) {
+      tot[e] = run;
+      counts[e] = run;
+    }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int o = 0;
-    for (int e = 0; e < E; ++e) {
-      offsets[e] = o;
-      o += tot[e];
+  if (act) {
+    int run = part_base[warp][lane];
+    int b = b_lo;
+    for (; b + 8 <= b_hi; b += 8) {
+      int v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = block_counts[(int64_t)(b + j) * E + e];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        block_counts[(int64_t)(b + j) * E + e] = run;  // the block's base within e
+        run += v[j];
+      }
     }
-    offsets[E] = o;
+    for (; b < b_hi; ++b) {
+      const int c = block_counts[(int64_t)b * E + e];
+      block_counts[(int64_t)b * E + e] = run;
+      run += c;
+    }
+  }
+  if (warp == 0) {  // offsets: exclusive scan of the totals, 32 experts at a time
+    int carry = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int v = e0 + lane < E ? tot[e0 + lane] : 0;
+      int inc = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+      }
+      if (e0 + lane < E) offsets[e0 + lane] = carry + inc - v;
+      carry += __shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0) offsets[E] = carry;
   }
 }
 

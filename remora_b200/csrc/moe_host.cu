@@ -41,7 +41,7 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
   } else {
     while (le < E) le *= 2;
   }
-  auto tokens_per_block = [&](int rt) { return (int64_t)(kRouterThreads / 32) * (32 / le) * rt; };
+  auto tokens_per_block = [&](int rt) { return (int64_t)8 * (32 / le) * rt; };
   int rt = 1;
   for (int c = 16; c > 1; c /= 2)
     if (c <= le && c * epl <= 32 &&
@@ -55,30 +55,30 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
   auto launch = [&](auto kern) -> int {
     if (smem > 48 * 1024)
       RB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<(unsigned)grid, kRouterThreads, smem, st>>>(static_cast<const uint16_t*>(x),
+    kern<<<(unsigned)grid, 256, smem, st>>>(static_cast<const uint16_t*>(x),
                                                        static_cast<const uint16_t*>(wr), (int)T,
                                                        (int)D, E, k, le, idx, w);
     return REMORA_B200_OK;
   };
   int rc;
   switch (epl * 100 + rt) {
-    case 101: rc = launch(k_router_topk<1, 1>); break;
-    case 102: rc = launch(k_router_topk<2, 1>); break;
-    case 104: rc = launch(k_router_topk<4, 1>); break;
-    case 108: rc = launch(k_router_topk<8, 1>); break;
-    case 116: rc = launch(k_router_topk<16, 1>); break;
-    case 201: rc = launch(k_router_topk<1, 2>); break;
-    case 202: rc = launch(k_router_topk<2, 2>); break;
-    case 204: rc = launch(k_router_topk<4, 2>); break;
-    case 208: rc = launch(k_router_topk<8, 2>); break;
-    case 216: rc = launch(k_router_topk<16, 2>); break;
-    case 401: rc = launch(k_router_topk<1, 4>); break;
-    case 402: rc = launch(k_router_topk<2, 4>); break;
-    case 404: rc = launch(k_router_topk<4, 4>); break;
-    case 408: rc = launch(k_router_topk<8, 4>); break;
-    case 801: rc = launch(k_router_topk<1, 8>); break;
-    case 802: rc = launch(k_router_topk<2, 8>); break;
-    default: rc = launch(k_router_topk<4, 8>); break;
+    case 101: rc = launch(k_router_topk<1, 1, 8>); break;
+    case 102: rc = launch(k_router_topk<2, 1, 8>); break;
+    case 104: rc = launch(k_router_topk<4, 1, 8>); break;
+    case 108: rc = launch(k_router_topk<8, 1, 8>); break;
+    case 116: rc = launch(k_router_topk<16, 1, 8>); break;
+    case 201: rc = launch(k_router_topk<1, 2, 8>); break;
+    case 202: rc = launch(k_router_topk<2, 2, 8>); break;
+    case 204: rc = launch(k_router_topk<4, 2, 8>); break;
+    case 208: rc = launch(k_router_topk<8, 2, 8>); break;
+    case 216: rc = launch(k_router_topk<16, 2, 8>); break;
+    case 401: rc = launch(k_router_topk<1, 4, 8>); break;
+    case 402: rc = launch(k_router_topk<2, 4, 8>); break;
+    case 404: rc = launch(k_router_topk<4, 4, 8>); break;
+    case 408: rc = launch(k_router_topk<8, 4, 8>); break;
+    case 801: rc = launch(k_router_topk<1, 8, 8>); break;
+    case 802: rc = launch(k_router_topk<2, 8, 8>); break;
+    default: rc = launch(k_router_topk<4, 8, 8>); break;
   }
   if (rc) return rc;
   RB_LAUNCH_CHECK();
@@ -103,7 +103,7 @@ int dispatch_launch(const int32_t* idx, int64_t T, int k, int E, int32_t* counts
   }
   k_dispatch_count<<<(unsigned)nb, kDispThreads, E * sizeof(int), st>>>(idx, n, E, block_counts);
   RB_LAUNCH_CHECK();
-  k_dispatch_scan<<<1, 256, E * sizeof(int), st>>>(block_counts, (int)nb, E, counts, offsets);
+  k_dispatch_scan<<<1, kScanThreads, 0, st>>>(block_counts, (int)nb, E, counts, offsets);
   RB_LAUNCH_CHECK();
   k_dispatch_scatter<<<(unsigned)nb, kDispThreads, 32 * E * sizeof(int), st>>>(
       idx, n, E, block_counts, offsets, perm, inv);

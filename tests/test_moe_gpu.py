@@ -58,6 +58,7 @@ def test_router_full_size_bit_exact(rb, orc, T, D, E, k):
 
 
 @pytest.mark.parametrize("T,k,E,mode", [(1000, 2, 8, "uniform"), (65536, 8, 64, "uniform"),
+                                        (100000, 8, 64, "skewed"), (70000, 16, 256, "uniform"),
                                         (3000, 2, 8, "one_expert"), (777, 4, 32, "skewed"),
                                         (1, 1, 4, "uniform"), (1024, 1, 3, "uniform")])
 def test_dispatch_bit_exact(rb, orc, T, k, E, mode):
