@@ -25,9 +25,12 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
   // of the SMs a block (RT <= LE, RT * EPL <= 32 accumulators).  The shared
   // memory delivers 16 (RT + EPL) bytes per 4 RT EPL FMAs, so larger blocks
   // of (tokens x experts) per lane are faster until the grid runs short.
-  // Measured on B200 (T, D, E): (8192, 2048, 64) 138 us with LE 16, EPL 4,
-  // RT 4; (65536, 2048, 64) 689 us with RT 8; (8192, 4096, 8) 99 us with LE 8,
-  // EPL 1, RT 2.
+  // Measured on B200 (T, D, E): (8192, 2048, 64) 134 us with LE 16, EPL 4,
+  // RT 4; (65536, 2048, 64) 660 us with RT 8.  A sweep of RT, EPL and warps
+  // per block found nothing faster for 64 experts (LE 32 with EPL 2 and RT
+  // 16, the largest register block, is 1.4-2x slower).  With 5-8 experts
+  // (LE 8, EPL 1) blocks of 2 warps with RT 2 are fastest: (8192, 4096, 8)
+  // 84 us against 104 us with 8-warp blocks.
   int epl = 1, le = 1;
   if (E > 128) {
     epl = 8;
@@ -41,27 +44,33 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
   } else {
     while (le < E) le *= 2;
   }
-  auto tokens_per_block = [&](int rt) { return (int64_t)8 * (32 / le) * rt; };
+  const int warps = (le == 8 && epl == 1) ? 2 : 8;
+  auto tokens_per_block = [&](int rt) { return (int64_t)warps * (32 / le) * rt; };
   int rt = 1;
-  for (int c = 16; c > 1; c /= 2)
-    if (c <= le && c * epl <= 32 &&
-        4 * ((T + tokens_per_block(c) - 1) / tokens_per_block(c)) >= 3 * (int64_t)num_sms()) {
-      rt = c;
-      break;
-    }
+  if (warps == 2) {
+    rt = 2;
+  } else {
+    for (int c = 16; c > 1; c /= 2)
+      if (c <= le && c * epl <= 32 &&
+          4 * ((T + tokens_per_block(c) - 1) / tokens_per_block(c)) >= 3 * (int64_t)num_sms()) {
+        rt = c;
+        break;
+      }
+  }
   const int64_t tpb = tokens_per_block(rt);
   const size_t smem = (size_t)(tpb + le * epl) * kRowPadF * 4;
   const int64_t grid = (T + tpb - 1) / tpb;
   auto launch = [&](auto kern) -> int {
     if (smem > 48 * 1024)
       RB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kern<<<(unsigned)grid, 256, smem, st>>>(static_cast<const uint16_t*>(x),
+    kern<<<(unsigned)grid, warps * 32, smem, st>>>(static_cast<const uint16_t*>(x),
                                                        static_cast<const uint16_t*>(wr), (int)T,
                                                        (int)D, E, k, le, idx, w);
     return REMORA_B200_OK;
   };
   int rc;
-  switch (epl * 100 + rt) {
+  switch (warps == 2 ? -1 : epl * 100 + rt) {
+    case -1: rc = launch(k_router_topk<2, 1, 2>); break;
     case 101: rc = launch(k_router_topk<1, 1, 8>); break;
     case 102: rc = launch(k_router_topk<2, 1, 8>); break;
     case 104: rc = launch(k_router_topk<4, 1, 8>); break;
