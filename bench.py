@@ -51,9 +51,11 @@ NCU_TRAFFIC_BYTES = {
     "gemm_8192": 1140578560,  # profiles/gemm_bf16_8192_dram.md
     "gemm_batched": None,
     "elementwise": None,
-    "moe_swiglu_5": None,
+    "moe_swiglu_5": 4612174000,  # profiles/grouped_gemm_swiglu_65536x2048_e64_dram.md
     "moe_swiglu_4": None,
-    "moe_ep_experts": None,
+    # one-rank capture of the merged expert kernel at the per-rank shape of the 8-GPU
+    # layer (65536 rows): profiles/moe_ep_experts_p1_8x65536_full.md
+    "moe_ep_experts": 1321200000,
 }
 
 MOE_CONFIGS = {
