@@ -750,7 +750,7 @@ def bench_elementwise(args, world, rank, local):
     gbs_local = 12.0 * n / (ms_local * 1e-3) / 1e9
     roof = {"bound": "hbm", "achieved": gbs_local, "peak": peaks["hbm_gbs"], "unit": "GB/s",
             "frac": gbs_local / peaks["hbm_gbs"], "peak_source": src,
-            "traffic": NCU_TRAFFIC_BYTES.get("elementwise"), "kernel": "rb::ew::k_scale_add_exp_v4",
+            "traffic": NCU_TRAFFIC_BYTES.get("elementwise"), "kernel": "rb::k_scale_add_exp_v4",
             "kernel_ms": ms_local}
     return _line(args, world, bytes_step / (ms * 1e-3) / 1e9, "GB/s", ms, "weak", "f32",
                  "synthetic (seeded N(0,1) f32)", roof,

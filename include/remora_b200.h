@@ -90,6 +90,15 @@ typedef struct remora_b200_report {
  * simple_moe.mlir:16, with bf16 operands). */
 int remora_b200_recognise(const char* test);
 
+/* The launch plan of a recognised program, written to out (NUL-terminated,
+ * at most out_bytes): the entry points it calls and, for each, its kernels
+ * with grid x block, dynamic shared memory and argument shapes.  This is
+ * what `remora-b200 --emit-ptx` prints in place of the NVVM PTX that
+ * remora's --emit-ptx prints (compiler/gpu.cpp:222-224): the kernels here
+ * are hand-written sm_100a code, not generated.  Needs no GPU (the SM count
+ * defaults to 148 when no device is visible). */
+int remora_b200_launch_plan(const char* test, const char* config, char* out, size_t out_bytes);
+
 /* Runs the recognised program end to end on `o->device`: allocates its own
  * buffers, fills the inputs, launches, times and validates.  Replaces
  * launchElementwiseOnGpu (gpu_tests.cpp:35-95), which allocated, filled

@@ -63,6 +63,8 @@ _SIGNATURES = {
     "remora_b200_version": ([], I),
     "remora_b200_recognise": ([ctypes.c_char_p], I),
     "remora_b200_run_test": ([ctypes.c_char_p, ctypes.POINTER(Opts), ctypes.POINTER(Report)], I),
+    "remora_b200_launch_plan": ([ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p,
+                                 ctypes.c_size_t], I),
     "remora_b200_relu_bias_f32": ([P, P, P, I64, I64, P], I),
     "remora_b200_scale_add_exp_f32": ([P, P, P, I64, F, P], I),
     "remora_b200_gemm_bf16": ([P, P, P, I64, I64, I64, I64, I64, I64, I64, I64, I64, I64, I, P], I),
@@ -165,6 +167,15 @@ def run_test(test: str, device: int = 0, seed: int = 42, iters: int = 1, warmup:
     if rc != OK:
         raise RemoraError(rc, last_error())
     return rep
+
+
+def launch_plan(test: str, config: str | None = None) -> str:
+    """The kernels a recognised program launches, with their geometry
+    (what `remora-b200 --emit-ptx` prints)."""
+    buf = ctypes.create_string_buffer(8192)
+    _check(lib().remora_b200_launch_plan(test.encode(), config.encode() if config else None,
+                                         buf, len(buf)))
+    return buf.value.decode()
 
 
 # -------------------------------------------------------------- elementwise

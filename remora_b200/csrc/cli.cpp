@@ -108,11 +108,17 @@ int main(int argc, char** argv) {
                  test.c_str());
     return 1;
   }
-  if (emit_ptx && !run_gpu) {
-    std::printf("kernel path: remora_b200 '%s'%s%s (hand-written sm_100a kernels; no PTX is "
-                "generated)\n",
-                test.c_str(), config.empty() ? "" : " config ", config.c_str());
-    return 0;
+  if (emit_ptx) {
+    // remora prints the NVVM PTX here (gpu.cpp:222-224); this backend's kernels are
+    // hand-written, so it prints the launch plan: entry points, kernels, geometry
+    static char plan[16384];
+    if (remora_b200_launch_plan(test.c_str(), config.empty() ? nullptr : config.c_str(), plan,
+                                sizeof(plan)) != REMORA_B200_OK) {
+      std::fprintf(stderr, "remora_b200: %s\n", remora_b200_last_error());
+      return 1;
+    }
+    std::printf("%s", plan);
+    if (!run_gpu) return 0;
   }
   if (no_execute) return 0;
   o.config = config.empty() ? nullptr : config.c_str();

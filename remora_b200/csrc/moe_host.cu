@@ -9,17 +9,15 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 inline int64_t dispatch_blocks(int64_t n) { return (n + kDispThreads - 1) / kDispThreads; }
 
-int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, int k,
-                  int32_t* idx, float* w, cudaStream_t st) {
-  RB_CHECK_ARG(T >= 0 && D > 0 && E >= 1 && E <= GMaxE && k >= 1 && k <= 16 && k <= E,
-               "router: unsupported sizes (T=%lld D=%lld E=%d k=%d)", (long long)T,
-               (long long)D, E, k);
-  RB_CHECK_ARG(D % 8 == 0, "router: d_model must be a multiple of 8");
-  if (T == 0) return REMORA_B200_OK;
-  RB_CHECK_ARG(x && wr && idx && w, "router: null pointer");
-  RB_CHECK_ARG(aligned16(x), "router: x must be 16-byte aligned");
-  RB_CHECK_ARG(T < (1ll << 31) && D < (1ll << 31), "router: sizes exceed 2^31");
-  RB_CHECK_ARG(E % 8 == 0 || E <= 128, "router: E=%d must be a multiple of 8 above 128", E);
+// Router tile: lanes per token group LE, experts per lane EPL, tokens per
+// lane RT, warps per block, and the launch geometry that follows.
+struct RouterPlan {
+  int le, epl, rt, warps;
+  int64_t tpb, grid;
+  size_t smem;
+};
+
+RouterPlan router_plan(int64_t T, int E) {
   // Lanes per token group LE (a power of two) and experts per lane EPL with
   // LE * EPL >= E; tokens per lane RT as large as still leaves at least 3/4
   // of the SMs a block (RT <= LE, RT * EPL <= 32 accumulators).  The shared
@@ -57,9 +55,32 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
         break;
       }
   }
-  const int64_t tpb = tokens_per_block(rt);
-  const size_t smem = (size_t)(tpb + le * epl) * kRowPadF * 4;
-  const int64_t grid = (T + tpb - 1) / tpb;
+  RouterPlan p;
+  p.le = le;
+  p.epl = epl;
+  p.rt = rt;
+  p.warps = warps;
+  p.tpb = tokens_per_block(rt);
+  p.smem = (size_t)(p.tpb + le * epl) * kRowPadF * 4;
+  p.grid = (T + p.tpb - 1) / p.tpb;
+  return p;
+}
+
+int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, int k,
+                  int32_t* idx, float* w, cudaStream_t st) {
+  RB_CHECK_ARG(T >= 0 && D > 0 && E >= 1 && E <= GMaxE && k >= 1 && k <= 16 && k <= E,
+               "router: unsupported sizes (T=%lld D=%lld E=%d k=%d)", (long long)T,
+               (long long)D, E, k);
+  RB_CHECK_ARG(D % 8 == 0, "router: d_model must be a multiple of 8");
+  if (T == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(x && wr && idx && w, "router: null pointer");
+  RB_CHECK_ARG(aligned16(x), "router: x must be 16-byte aligned");
+  RB_CHECK_ARG(T < (1ll << 31) && D < (1ll << 31), "router: sizes exceed 2^31");
+  RB_CHECK_ARG(E % 8 == 0 || E <= 128, "router: E=%d must be a multiple of 8 above 128", E);
+  const RouterPlan pl = router_plan(T, E);
+  const int le = pl.le, epl = pl.epl, rt = pl.rt, warps = pl.warps;
+  const size_t smem = pl.smem;
+  const int64_t grid = pl.grid;
   auto launch = [&](auto kern) -> int {
     if (smem > 48 * 1024)
       RB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

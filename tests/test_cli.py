@@ -43,12 +43,31 @@ def test_usage_and_missing_file(cli, tmp_path):
     assert r.returncode == 1 and "Failed to parse" in r.stderr
 
 
-@pytest.mark.parametrize("sig,kind", [("elementwise", "elementwise"),
-                                      ("projection", "projection"),
-                                      ("moe_simple", "moe"), ("moe_mixtral", "moe")])
-def test_recognises_programs_without_gpu(cli, tmp_path, sig, kind):
+@pytest.mark.parametrize("sig,entry,kernels", [
+    ("elementwise", "remora_b200_relu_bias_f32", ["k_relu_bias_v4"]),
+    ("projection", "remora_b200_gemm_f32_exact", ["k_gemm_f32_exact"]),
+    ("moe_simple", "remora_b200_moe_layer_bf16(x bf16[8,32]",
+     ["k_router_topk", "k_dispatch_scan", "k_grouped_gemm<true>", "k_combine<2>"]),
+    ("moe_mixtral", "remora_b200_moe_layer_bf16(x bf16[512,4096]",
+     ["k_router_topk<2,1,2>", "k_gather_rows", "k_grouped_gemm<false>"])])
+def test_emit_ptx_prints_the_launch_plan_without_gpu(cli, tmp_path, sig, entry, kernels):
+    """--emit-ptx (compiler/gpu.cpp:222-224 prints the NVVM PTX) prints the
+    recognised program's entry points and kernels with their geometry."""
     r = _run(cli, "--emit-ptx", tmp_path=tmp_path, sig=sig)
-    assert r.returncode == 0 and f"'{kind}'" in r.stdout
+    assert r.returncode == 0, r.stderr
+    assert entry in r.stdout and all(k in r.stdout for k in kernels), r.stdout
+    assert "grid" in r.stdout and "block" in r.stdout
+
+
+def test_launch_plan_rejects_unknown_kind_and_small_buffer():
+    import ctypes
+
+    import remora_b200 as rb
+
+    buf = ctypes.create_string_buffer(16)
+    assert rb.lib().remora_b200_launch_plan(b"softmax_v2", None, buf, 16) == rb.ERR_UNSUPPORTED
+    assert rb.lib().remora_b200_launch_plan(b"moe", b"5", buf, 16) == rb.ERR_INVALID
+    assert "gemm_bf16" in rb.launch_plan("gemm", "1024x512x256")
 
 
 def test_unknown_kind_fails(cli, tmp_path):
