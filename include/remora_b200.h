@@ -87,7 +87,8 @@ typedef struct remora_b200_report {
  * Kinds: "elementwise" (gpu_tests.cpp:35-95), "projection"
  * (cpu_tests.cpp:65-97), "elementwise_chain", "gemm", "attention", "moe"
  * (configs "4", "5", "mixtral" = mixtral_moe_layer.mlir:8, "simple" =
- * simple_moe.mlir:16, with bf16 operands). */
+ * simple_moe.mlir:16, "hetero" = heterogeneous_moe_layer.mlir:66, with
+ * bf16 operands). */
 int remora_b200_recognise(const char* test);
 
 /* The launch plan of a recognised program, written to out (NUL-terminated,
@@ -261,6 +262,46 @@ size_t remora_b200_moe_workspace_bytes(int64_t T, int64_t D, int64_t F, int E, i
 int remora_b200_moe_layer_bf16(const void* x, const void* wr, const void* wg, const void* wu,
                                const void* wd, void* out, int64_t T, int64_t D, int64_t F, int E,
                                int k, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Heterogeneous MoE: experts of different FFN widths
+ * (mlir/stablehlo/heterogeneous_moe_layer.mlir:66-212, one [1, D, F_e] weight
+ * tensor per expert, :66-100).  E <= 16 experts; wg, wu, wd are host arrays
+ * of E device pointers (expert e: wg[e], wu[e] bf16 [D, F_e], wd[e] bf16
+ * [F_e, D]); F is a host array of the E widths.
+ * --------------------------------------------------------------------- */
+
+/* h[r, :F_e] = silu(xs[r] . wg[e]) * (xs[r] . wu[e]) for the rows of expert e
+ * (offsets[e] <= r < offsets[e+1], offsets on the device).  h [rows, ldh],
+ * ldh >= every F_e; F_e % 32 == 0, D % 8 == 0.  All experts' tiles run in
+ * one persistent launch: the tile list carries each expert's own column
+ * count and weight tensor map. */
+int remora_b200_grouped_gemm_swiglu_var_bf16(const void* xs, const void* const* wg,
+                                             const void* const* wu, void* h, int64_t ldh,
+                                             const int32_t* offsets, int64_t rows, int64_t D,
+                                             const int64_t* F, int E, void* stream);
+
+/* y[r, :] = h[r, :F_e] . wd[e] for the rows of expert e: the contraction
+ * length is each expert's own F_e (a multiple of 64, or equal to ldh). */
+int remora_b200_grouped_gemm_var_bf16(const void* h, int64_t ldh, const void* const* wd, void* y,
+                                      const int32_t* offsets, int64_t rows, const int64_t* F,
+                                      int64_t D, int E, void* stream);
+
+/* Bytes of device workspace remora_b200_moe_hetero_layer_bf16 needs (0 for
+ * sizes it rejects). */
+size_t remora_b200_moe_hetero_workspace_bytes(int64_t T, int64_t D, const int64_t* F, int E,
+                                              int k);
+
+/* The heterogeneous layer: router (bit-exact top-k as the uniform layer),
+ * dispatch, gather, the two variable-width grouped GEMMs, combine.  With
+ * k = 1 the combine weight is softmax over one logit = 1, so out[t] is the
+ * selected expert's output, as the program's one-hot combine gives
+ * (:210-225).  D % 32 == 0; every F_e a positive multiple of 64. */
+int remora_b200_moe_hetero_layer_bf16(const void* x, const void* wr, const void* const* wg,
+                                      const void* const* wu, const void* const* wd,
+                                      const int64_t* F, void* out, int64_t T, int64_t D, int E,
+                                      int k, void* workspace, size_t workspace_bytes,
+                                      void* stream);
 
 /* ------------------------------------------------------------------------
  * Expert-parallel MoE over NVLink peer memory (P <= 8 ranks, one per GPU).

@@ -331,3 +331,23 @@ def moe_layer_bf16(x, wr, wg, wu, wd, k: int, tokens: np.ndarray | None = None):
     inv_local = np.arange(tokens.shape[0] * k, dtype=np.int32).reshape(-1, k)
     out[:] = combine(ysel, inv_local, w[tokens])
     return idx, w, counts, offsets, perm, inv, out
+
+
+def moe_hetero_layer_bf16(x, wr, wg: list, wu: list, wd: list, k: int,
+                          tokens: np.ndarray | None = None):
+    """The heterogeneous MoE layer (heterogeneous_moe_layer.mlir:66-212):
+    expert e has its own weights wg[e], wu[e] [D, F_e] and wd[e] [F_e, D].
+    Routing and dispatch over every token; expert FFN and combine for the
+    listed tokens (all if None).  Returns (idx, w, out_rows bf16)."""
+    T, D = x.shape
+    idx, w = router_topk(x, wr, k)
+    if tokens is None:
+        tokens = np.arange(T)
+    tokens = np.asarray(tokens, np.int64)
+    ysel = np.empty((tokens.shape[0] * k, D), np.uint16)
+    for e in np.unique(idx[tokens]):
+        sel_t, sel_j = np.nonzero(idx[tokens] == e)
+        _, y, _ = expert_ffn(x[tokens[sel_t]], wg[e], wu[e], wd[e])
+        ysel[sel_t * k + sel_j] = y
+    inv_local = np.arange(tokens.shape[0] * k, dtype=np.int32).reshape(-1, k)
+    return idx, w, combine(ysel, inv_local, w[tokens])

@@ -103,6 +103,11 @@ _SIGNATURES = {
     "remora_b200_nccl_comm_init": ([ctypes.POINTER(ctypes.c_void_p), I, P, I, I, I64], I),
     "remora_b200_nccl_comm_destroy": ([P, I64], I),
     "remora_b200_nccl_comm_abort": ([P], I),
+    "remora_b200_grouped_gemm_swiglu_var_bf16": ([P, P, P, P, I64, P, I64, I64, P, I, P], I),
+    "remora_b200_grouped_gemm_var_bf16": ([P, I64, P, P, P, I64, P, I64, I, P], I),
+    "remora_b200_moe_hetero_workspace_bytes": ([I64, I64, P, I, I], ctypes.c_size_t),
+    "remora_b200_moe_hetero_layer_bf16": ([P, P, P, P, P, P, P, I64, I64, I, I, P,
+                                           ctypes.c_size_t, P], I),
     "remora_b200_device_status": ([], I),
     "remora_b200_fill_normal": ([P, I64, I, U64, D, D, P], I),
     "remora_b200_fill_uniform": ([P, I64, I, U64, D, D, P], I),
@@ -419,6 +424,69 @@ def moe_layer(x: torch.Tensor, wr: torch.Tensor, wg: torch.Tensor, wu: torch.Ten
         wu.contiguous().data_ptr(), wd.contiguous().data_ptr(), out.data_ptr(), T, D, F, E, k,
         workspace.data_ptr(), workspace.numel(), _stream(x)))
     return out
+
+
+def _ptrs(ts):
+    return (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
+
+
+def _i64s(vals):
+    return (ctypes.c_int64 * len(vals))(*vals)
+
+
+def moe_hetero_layer(x: torch.Tensor, wr: torch.Tensor, wg: list, wu: list, wd: list, k: int,
+                     out: torch.Tensor | None = None,
+                     workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """MoE layer whose experts have their own FFN widths: wg[e], wu[e] bf16
+    [D, F_e], wd[e] bf16 [F_e, D] (heterogeneous_moe_layer.mlir)."""
+    _dev(x, wr, *wg, *wu, *wd)
+    _bf16(x, wr, *wg, *wu, *wd)
+    T, D = x.shape
+    E = len(wg)
+    if not (len(wu) == len(wd) == E == wr.shape[1]):
+        raise ValueError("one gate, up and down weight per expert")
+    F = [int(w.shape[1]) for w in wg]
+    wg, wu, wd = ([w.contiguous() for w in ws] for ws in (wg, wu, wd))
+    need = int(lib().remora_b200_moe_hetero_workspace_bytes(T, D, _i64s(F), E, k))
+    if need == 0:
+        raise ValueError("moe_hetero_layer: sizes rejected")
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=x.device)
+    out = torch.empty((T, D), dtype=torch.bfloat16, device=x.device) if out is None else out
+    _check(lib().remora_b200_moe_hetero_layer_bf16(
+        x.contiguous().data_ptr(), wr.contiguous().data_ptr(), _ptrs(wg), _ptrs(wu), _ptrs(wd),
+        _i64s(F), out.data_ptr(), T, D, E, k, workspace.data_ptr(), workspace.numel(),
+        _stream(x)))
+    return out
+
+
+def grouped_gemm_swiglu_var(xs, wg: list, wu: list, offsets, ldh: int | None = None):
+    """h[r, :F_e] = silu(xs[r] . wg[e]) * (xs[r] . wu[e]); h [rows, ldh]."""
+    _dev(xs, offsets, *wg, *wu)
+    _i32(offsets)
+    rows, D = xs.shape
+    F = [int(w.shape[1]) for w in wg]
+    ldh = ldh or max(F)
+    h = torch.zeros((rows, ldh), dtype=torch.bfloat16, device=xs.device)
+    _check(lib().remora_b200_grouped_gemm_swiglu_var_bf16(
+        xs.contiguous().data_ptr(), _ptrs([w.contiguous() for w in wg]),
+        _ptrs([w.contiguous() for w in wu]), h.data_ptr(), ldh, offsets.data_ptr(), rows, D,
+        _i64s(F), len(wg), _stream(xs)))
+    return h
+
+
+def grouped_gemm_var(h, wd: list, offsets):
+    """y[r, :] = h[r, :F_e] . wd[e] for the rows of expert e (wd[e] [F_e, D])."""
+    _dev(h, offsets, *wd)
+    _i32(offsets)
+    rows, ldh = h.shape
+    F = [int(w.shape[0]) for w in wd]
+    D = int(wd[0].shape[1])
+    y = torch.empty((rows, D), dtype=torch.bfloat16, device=h.device)
+    _check(lib().remora_b200_grouped_gemm_var_bf16(
+        h.contiguous().data_ptr(), ldh, _ptrs([w.contiguous() for w in wd]), y.data_ptr(),
+        offsets.data_ptr(), rows, _i64s(F), D, len(wd), _stream(h)))
+    return y
 
 
 def synchronize_and_check(device=None) -> None:

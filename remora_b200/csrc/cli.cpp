@@ -38,6 +38,10 @@ Program recognise_program(const std::string& text) {
   // simple_attention_projection.mlir:4
   if (has("tensor<1x512x768xf32>") && has("tensor<768x768xf32>"))
     return {"projection", nullptr, "dot_general x . w, f32 [1,512,768] x [768,768]"};
+  // heterogeneous_moe_layer.mlir:66-100: one [1, D, F_e] weight per expert
+  if (has("tensor<512x4096xf32>") && has("tensor<1x4096x14336xf32>") &&
+      has("tensor<1x4096x2048xf32>"))
+    return {"moe", "hetero", "heterogeneous MoE layer T=512 D=4096 F=14336/8192/4096/2048 E=8 top-1"};
   // mixtral_moe_layer.mlir:8
   if (has("tensor<512x4096xf32>") && has("tensor<8x4096x14336xf32>"))
     return {"moe", "mixtral", "MoE layer T=512 D=4096 F=14336 E=8 top-2"};

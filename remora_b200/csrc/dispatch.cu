@@ -4,6 +4,7 @@
 // launches through the per-op C ABI, times with CUDA events and validates on
 // the host, as launchElementwiseOnGpu (gpu_tests.cpp:35-95) did -- except
 // that a validation failure is a non-zero status here.
+#include <algorithm>
 #include <cmath>
 #include <string>
 #include <vector>
@@ -318,31 +319,55 @@ static int run_attention(const remora_b200_opts* o, remora_b200_report* r, cudaS
 // T=8 D=32 F=64 E=2 top-1).  Tokens N(0,1), weights N(0,0.02), seeded.
 // Validation on up to 16 sampled tokens: router indices exactly as the
 // increasing-d fp32 loop nest gives them, layer output normwise <= 2e-2.
+// config "hetero": heterogeneous_moe_layer.mlir:66-212 (T=512, D=4096,
+// experts of F 14336, 14336, 8192, 8192, 4096, 4096, 2048, 2048, top-1)
+// through remora_b200_moe_hetero_layer_bf16; expert e's weights follow
+// expert e-1's in one buffer per kind.
 static int run_moe(const remora_b200_opts* o, remora_b200_report* r, cudaStream_t st) {
   int64_t T = 8192, D = 4096, F = 14336;
   int E = 8, k = 2;
   std::string c = o && o->config ? o->config : "4";
+  std::vector<int64_t> Fe;
   if (c == "5") { T = 65536; D = 2048; F = 1536; E = 64; k = 8; }
   else if (c == "mixtral") { T = 512; }
   else if (c == "simple") { T = 8; D = 32; F = 64; E = 2; k = 1; }
+  else if (c == "hetero") {
+    T = 512; k = 1;
+    Fe = {14336, 14336, 8192, 8192, 4096, 4096, 2048, 2048};
+  }
   else if (c != "4") return fail(REMORA_B200_ERR_INVALID, "moe: unknown config '%s'", c.c_str());
+  const bool hetero = !Fe.empty();
+  if (!hetero) Fe.assign(E, F);
+  std::vector<int64_t> off(E + 1, 0);  // element offset of expert e's weights
+  for (int e = 0; e < E; ++e) off[e + 1] = off[e] + D * Fe[e];
+  const int64_t wtot = off[E];
   const uint64_t seed = o && o->seed ? o->seed : 42;
   DevBuf x, wr, wg, wu, wd, out, ws, idx, w;
-  const size_t wsb = remora_b200_moe_workspace_bytes(T, D, F, E, k);
+  const size_t wsb = hetero ? remora_b200_moe_hetero_workspace_bytes(T, D, Fe.data(), E, k)
+                            : remora_b200_moe_workspace_bytes(T, D, F, E, k);
   int rc;
-  if ((rc = x.alloc(T * D * 2)) || (rc = wr.alloc(D * E * 2)) || (rc = wg.alloc(E * D * F * 2)) ||
-      (rc = wu.alloc(E * D * F * 2)) || (rc = wd.alloc(E * F * D * 2)) ||
+  if ((rc = x.alloc(T * D * 2)) || (rc = wr.alloc(D * E * 2)) || (rc = wg.alloc(wtot * 2)) ||
+      (rc = wu.alloc(wtot * 2)) || (rc = wd.alloc(wtot * 2)) ||
       (rc = out.alloc(T * D * 2)) || (rc = ws.alloc(wsb)) || (rc = idx.alloc(T * k * 4)) ||
       (rc = w.alloc(T * k * 4)))
     return rc;
   if ((rc = remora_b200_fill_normal(x.p, T * D, 1, stream_key(seed, 30), 0, 1, st)) ||
       (rc = remora_b200_fill_normal(wr.p, D * E, 1, stream_key(seed, 31), 0, 0.02, st)) ||
-      (rc = remora_b200_fill_normal(wg.p, E * D * F, 1, stream_key(seed, 32), 0, 0.02, st)) ||
-      (rc = remora_b200_fill_normal(wu.p, E * D * F, 1, stream_key(seed, 33), 0, 0.02, st)) ||
-      (rc = remora_b200_fill_normal(wd.p, E * F * D, 1, stream_key(seed, 34), 0, 0.02, st)))
+      (rc = remora_b200_fill_normal(wg.p, wtot, 1, stream_key(seed, 32), 0, 0.02, st)) ||
+      (rc = remora_b200_fill_normal(wu.p, wtot, 1, stream_key(seed, 33), 0, 0.02, st)) ||
+      (rc = remora_b200_fill_normal(wd.p, wtot, 1, stream_key(seed, 34), 0, 0.02, st)))
     return rc;
+  std::vector<const void*> pg(E), pu(E), pd(E);
+  for (int e = 0; e < E; ++e) {
+    pg[e] = (const uint16_t*)wg.p + off[e];
+    pu[e] = (const uint16_t*)wu.p + off[e];
+    pd[e] = (const uint16_t*)wd.p + off[e];
+  }
   double ms = 0;
   rc = time_iters(o, st, [&] {
+    if (hetero)
+      return remora_b200_moe_hetero_layer_bf16(x.p, wr.p, pg.data(), pu.data(), pd.data(),
+                                               Fe.data(), out.p, T, D, E, k, ws.p, wsb, st);
     return remora_b200_moe_layer_bf16(x.p, wr.p, wg.p, wu.p, wd.p, out.p, T, D, F, E, k, ws.p,
                                       wsb, st);
   }, &ms);
@@ -362,7 +387,8 @@ static int run_moe(const remora_b200_opts* o, remora_b200_report* r, cudaStream_
     RB_CUDA(cudaMemcpy(hidx.data(), idx.p, hidx.size() * 4, cudaMemcpyDeviceToHost));
     const int ns = (int)std::min<int64_t>(T, 16);
     std::vector<std::vector<uint16_t>> eg(E), eu(E), ed(E);
-    std::vector<double> ref(D), hrow(F), g(F), u(F);
+    const int64_t Fmax = *std::max_element(Fe.begin(), Fe.end());
+    std::vector<double> ref(D), hrow(Fmax), g(Fmax), u(Fmax);
     double worst = 0, scale = 0;
     for (int si = 0; si < ns; ++si) {
       const int64_t t = (int64_t)(host_mix64(stream_key(seed, 97) + si) % (uint64_t)T);
@@ -389,11 +415,12 @@ static int run_moe(const remora_b200_opts* o, remora_b200_report* r, cudaStream_
       std::fill(ref.begin(), ref.end(), 0.0);
       for (int j = 0; j < k; ++j) {
         const int ee = sel[j];
+        const int64_t F = Fe[ee];
         if (eg[ee].empty()) {
           eg[ee].resize(D * F); eu[ee].resize(D * F); ed[ee].resize(F * D);
-          RB_CUDA(cudaMemcpy(eg[ee].data(), (uint16_t*)wg.p + ee * D * F, D * F * 2, cudaMemcpyDeviceToHost));
-          RB_CUDA(cudaMemcpy(eu[ee].data(), (uint16_t*)wu.p + ee * D * F, D * F * 2, cudaMemcpyDeviceToHost));
-          RB_CUDA(cudaMemcpy(ed[ee].data(), (uint16_t*)wd.p + ee * F * D, F * D * 2, cudaMemcpyDeviceToHost));
+          RB_CUDA(cudaMemcpy(eg[ee].data(), pg[ee], D * F * 2, cudaMemcpyDeviceToHost));
+          RB_CUDA(cudaMemcpy(eu[ee].data(), pu[ee], D * F * 2, cudaMemcpyDeviceToHost));
+          RB_CUDA(cudaMemcpy(ed[ee].data(), pd[ee], F * D * 2, cudaMemcpyDeviceToHost));
         }
         std::fill(g.begin(), g.end(), 0.0);
         std::fill(u.begin(), u.end(), 0.0);
@@ -420,7 +447,10 @@ static int run_moe(const remora_b200_opts* o, remora_b200_report* r, cudaStream_
     e.max_abs = worst;
     e.max_rel = scale > 0 ? worst / scale : worst;
   }
-  finish(r, ms, 6.0 * D * F * T * k, e, 2e-2, o ? o->validate : 0, "moe layer bf16", "TFLOP/s");
+  double fsum = 0;  // expert FLOP as if the rows spread evenly over the experts
+  for (int64_t f : Fe) fsum += (double)f;
+  finish(r, ms, 6.0 * D * (fsum / E) * T * k, e, 2e-2, o ? o->validate : 0,
+         hetero ? "heterogeneous moe layer bf16" : "moe layer bf16", "TFLOP/s");
   if (o && o->validate && !idx_ok) {
     r->passed = 0;
     snprintf(r->detail, sizeof(r->detail), "moe layer: router indices differ from the loop nest");

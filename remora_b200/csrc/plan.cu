@@ -68,6 +68,26 @@ void moe_plan(Text& t, int64_t T, int64_t D, int64_t F, int E, int k) {
         (long long)std::min<int64_t>((T + 7) / 8, (int64_t)num_sms() * 16));
 }
 
+void hetero_plan(Text& t) {
+  using namespace moe;
+  const int64_t T = 512, D = 4096;
+  const int64_t F[8] = {14336, 14336, 8192, 8192, 4096, 4096, 2048, 2048};
+  const RouterPlan rp = router_plan(T, 8);
+  t.add("remora_b200_moe_hetero_layer_bf16(x bf16[512,4096], wr bf16[4096,8], wg[e]/wu[e] "
+        "bf16[4096,F_e], wd[e] bf16[F_e,4096], F_e = 14336 14336 8192 8192 4096 4096 2048 2048, "
+        "out bf16[512,4096]), top-1, workspace %zu B\n",
+        remora_b200_moe_hetero_workspace_bytes(T, D, F, 8, 1));
+  t.add("  rb::moe::k_router_topk<%d,%d,%d>  grid %lld x block %d, smem %zu B\n", rp.rt, rp.epl,
+        rp.warps, (long long)rp.grid, rp.warps * 32, rp.smem);
+  t.add("  rb::moe::k_dispatch_count / k_dispatch_scan / k_dispatch_scatter  grid 1 / 1 / 1\n");
+  t.add("  rb::moe::k_gather_rows  grid 64 x block 256 (512 rows of 4096 bf16)\n");
+  t.add("  rb::moe::k_grouped_var<true>  grid %d x block %d, smem %u B (per-expert tensor maps; "
+        "column tiles of 128 up to each F_e)\n", num_sms(), GThreads, GSmemBytes);
+  t.add("  rb::moe::k_grouped_var<false>  grid %d x block %d, smem %u B (K = F_e per expert)\n",
+        num_sms(), GThreads, GSmemBytes);
+  t.add("  rb::moe::k_combine<2>  grid 64 x block 256\n");
+}
+
 }  // namespace plan
 }  // namespace rb
 
@@ -125,6 +145,8 @@ extern "C" int remora_b200_launch_plan(const char* test, const char* config, cha
       moe_plan(t, 512, 4096, 14336, 8, 2);
     else if (c == "simple")
       moe_plan(t, 8, 32, 64, 2, 1);
+    else if (c == "hetero")
+      hetero_plan(t);
     else
       return fail(REMORA_B200_ERR_INVALID, "launch_plan: unknown moe config '%s'", c.c_str());
   } else {

@@ -2,7 +2,7 @@
 
     python -m remora_b200.profile_case <case> [--reps N] [--warmup W] [shape options]
 
-Cases: router, dispatch, gather, combine, swiglu, down, attention, gemm, layer.
+Cases: router, dispatch, gather, combine, swiglu, down, attention, gemm, layer, hetero.
 Each run fills its inputs with the seeded generator, launches the kernel
 `warmup` times, then `reps` times between CUDA events on the current
 stream, and prints one line: case, shape, time per launch, and the
@@ -93,6 +93,17 @@ def build_case(a):
         ws = torch.empty(rb.moe_workspace_bytes(T, D, F, E, k), dtype=torch.uint8, device="cuda")
         return (lambda: rb.moe_layer(x, wr, wg, wu, wd, k, out=out, workspace=ws),
                 f"MoE layer T={T} D={D} F={F} E={E} k={k}", 6.0 * T * k * D * F, "FLOP")
+    if a.case == "hetero":
+        # heterogeneous_moe_layer.mlir: 8 experts of F 14336 x2, 8192 x2, 4096 x2, 2048 x2
+        Fs = [14336, 14336, 8192, 8192, 4096, 4096, 2048, 2048]
+        x, wr, _, _ = _routing(T, D, len(Fs), k)
+        wg = [_bf16((D, f), 32 + 10 * e, 0.02) for e, f in enumerate(Fs)]
+        wu = [_bf16((D, f), 33 + 10 * e, 0.02) for e, f in enumerate(Fs)]
+        wd = [_bf16((f, D), 34 + 10 * e, 0.02) for e, f in enumerate(Fs)]
+        out = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
+        return (lambda: rb.moe_hetero_layer(x, wr, wg, wu, wd, k, out=out),
+                f"heterogeneous MoE layer T={T} D={D} F={Fs} top-{k}",
+                6.0 * T * k * D * sum(Fs) / len(Fs), "FLOP")
     raise SystemExit(f"unknown case {a.case}")
 
 

@@ -16,6 +16,9 @@ SIGS = {
                   "%arg2: tensor<2x32x64xf32>, %arg3: tensor<2x32x64xf32>, %arg4: tensor<2x64x32xf32>)",
     "moe_mixtral": "func.func public @main(%arg0: tensor<512x4096xf32>, %arg1: tensor<4096x8xf32>, "
                    "%arg2: tensor<8x4096x14336xf32>, %arg3: tensor<8x4096x14336xf32>)",
+    "moe_hetero": "func.func public @main(%tokens : tensor<512x4096xf32>, %router_w : "
+                  "tensor<4096x8xf32>, %wg_0 : tensor<1x4096x14336xf32>, %wg_6 : "
+                  "tensor<1x4096x2048xf32>)",
 }
 
 
@@ -49,7 +52,9 @@ def test_usage_and_missing_file(cli, tmp_path):
     ("moe_simple", "remora_b200_moe_layer_bf16(x bf16[8,32]",
      ["k_router_topk", "k_dispatch_scan", "k_grouped_gemm<true>", "k_combine<2>"]),
     ("moe_mixtral", "remora_b200_moe_layer_bf16(x bf16[512,4096]",
-     ["k_router_topk<2,1,2>", "k_gather_rows", "k_grouped_gemm<false>"])])
+     ["k_router_topk<2,1,2>", "k_gather_rows", "k_grouped_gemm<false>"]),
+    ("moe_hetero", "remora_b200_moe_hetero_layer_bf16",
+     ["k_grouped_var<true>", "k_grouped_var<false>", "F_e = 14336 14336 8192"])])
 def test_emit_ptx_prints_the_launch_plan_without_gpu(cli, tmp_path, sig, entry, kernels):
     """--emit-ptx (compiler/gpu.cpp:222-224 prints the NVVM PTX) prints the
     recognised program's entry points and kernels with their geometry."""
@@ -76,7 +81,7 @@ def test_unknown_kind_fails(cli, tmp_path):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("sig", ["elementwise", "projection", "moe_simple"])
+@pytest.mark.parametrize("sig", ["elementwise", "projection", "moe_simple", "moe_hetero"])
 def test_run_gpu_known_programs(cli, tmp_path, sig):
     r = _run(cli, "--run-gpu", tmp_path=tmp_path, sig=sig)
     assert r.returncode == 0, r.stdout + r.stderr
