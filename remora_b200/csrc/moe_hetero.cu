@@ -20,6 +20,8 @@ namespace rb {
 namespace moe {
 
 constexpr int kVarMaxE = 16;
+constexpr int64_t kSplitRows = 2048;  // down-GEMM K splits only for batches of <= this many rows
+constexpr int kMaxSplits = 8;
 
 // Per-expert weight tensor maps (2-D, [K_e rows x N_e columns], N contiguous).
 // Passed as one __grid_constant__ parameter (4 KB): TMA reads the maps where
@@ -33,28 +35,41 @@ struct VarShape {
   int E;
   int K[kVarMaxE];         // contraction length of expert e
   int N[kVarMaxE];         // output columns of expert e
+  int ks[kVarMaxE];        // K splits of expert e (1: no split)
   int64_t ldo;             // output row stride (elements)
   const int32_t* offsets;  // [E + 1] device: expert row ranges
   uint16_t* out;
+  float* partial;          // [max ks][prows][ldo] fp32 partial sums of split experts
+  int64_t prows;
 };
 
 struct VarTile {
-  int e, r0, r_end, n;
+  int e, r0, r_end, n, sp;
 };
 
-// Tile t -> (expert, row tile, column tile).  tp: tile prefix per expert,
-// mt: row tiles per expert, st / en: row range per expert.
-__device__ __forceinline__ VarTile var_tile(int E, const int* tp, const int* mt, const int* st,
-                                            const int* en, int t) {
+// Tile t -> (expert, row tile, column tile, K split).  tp: tile prefix per
+// expert, mt: row tiles per expert, tn: column tiles per expert, st / en:
+// row range per expert.  Row tile fastest, then column tile, then split.
+__device__ __forceinline__ VarTile var_tile(int E, const int* tp, const int* mt, const int* tn,
+                                            const int* st, const int* en, int t) {
   int e = 0;
   while (e + 1 < E && tp[e + 1] <= t) ++e;
   const int l = t - tp[e];
+  const int rest = l / mt[e];
   VarTile v;
   v.e = e;
   v.r0 = st[e] + (l % mt[e]) * GBM;
-  v.n = l / mt[e];
+  v.n = rest % tn[e];
+  v.sp = rest / tn[e];
   v.r_end = en[e];
   return v;
+}
+
+// k blocks [kb0, kb1) of split sp of a K of nkb blocks in ks splits
+__device__ __forceinline__ void split_range(int nkb, int ks, int sp, int* kb0, int* kb1) {
+  const int per = (nkb + ks - 1) / ks;
+  *kb0 = min(nkb, sp * per);
+  *kb1 = min(nkb, *kb0 + per);
 }
 
 template <bool kSwiGLU>
@@ -67,7 +82,8 @@ __global__ void __launch_bounds__(GThreads, 1)
   GSmem* sm = reinterpret_cast<GSmem*>(smem + GBarOffset);
   int* s_tp = reinterpret_cast<int*>(smem + GBarOffset + 256);  // [E + 1]
   int* s_mt = s_tp + (kVarMaxE + 1);
-  int* s_st = s_mt + kVarMaxE;
+  int* s_tn = s_mt + kVarMaxE;
+  int* s_st = s_tn + kVarMaxE;
   int* s_en = s_st + kVarMaxE;
   uint8_t* epi_stage_base = smem + GEpiOffset;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -81,8 +97,9 @@ __global__ void __launch_bounds__(GThreads, 1)
       s_st[e] = a;
       s_en[e] = b;
       s_mt[e] = (rows + GBM - 1) / GBM;
+      s_tn[e] = (s.N[e] + kCols - 1) / kCols;
       s_tp[e] = tp;
-      tp += s_mt[e] * ((s.N[e] + kCols - 1) / kCols);
+      tp += s_mt[e] * s_tn[e] * s.ks[e];
     }
     s_tp[s.E] = tp;
     for (int i = 0; i < GStages; ++i) {
@@ -114,12 +131,13 @@ __global__ void __launch_bounds__(GThreads, 1)
       int stage = 0, issued = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
-        const VarTile ti = var_tile(s.E, s_tp, s_mt, s_st, s_en, t);
+        const VarTile ti = var_tile(s.E, s_tp, s_mt, s_tn, s_st, s_en, t);
         const int n0 = ti.n * kCols;
-        const int nkb = (s.K[ti.e] + GBK - 1) / GBK;
+        int kb0, kb1;
+        split_range((s.K[ti.e] + GBK - 1) / GBK, s.ks[ti.e], ti.sp, &kb0, &kb1);
         const CUtensorMap* b0 = &maps.b0[ti.e];
         const CUtensorMap* b1 = &maps.b1[ti.e];
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&sm->empty[stage], phase ^ 1)) { *abort_flag = 1; break; }
           uint8_t* sa = smem + stage * GStageBytes;
           uint8_t* sb = sa + GABytes;
@@ -154,12 +172,13 @@ __global__ void __launch_bounds__(GThreads, 1)
       uint32_t phase = 0, acc_phase = 0;
       bool issued_any = false;
       for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
-        const VarTile ti = var_tile(s.E, s_tp, s_mt, s_st, s_en, t);
-        const int nkb = (s.K[ti.e] + GBK - 1) / GBK;
+        const VarTile ti = var_tile(s.E, s_tp, s_mt, s_tn, s_st, s_en, t);
+        int kb0, kb1;
+        split_range((s.K[ti.e] + GBK - 1) / GBK, s.ks[ti.e], ti.sp, &kb0, &kb1);
         if (!mbar_wait(&sm->tmem_empty[acc], acc_phase ^ 1)) { *abort_flag = 1; break; }
         tc_fence_after();
         const uint32_t d0 = tmem_base + acc * 256;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&sm->full[stage], phase)) { *abort_flag = 1; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * GStageBytes);
@@ -167,7 +186,7 @@ __global__ void __launch_bounds__(GThreads, 1)
 #pragma unroll
           for (int k = 0; k < GBK / 16; ++k) {
             const uint64_t adesc = smem_desc_sw128(sa + k * 32, 16, 1024);
-            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
             mma_bf16_ss(d0, adesc, smem_desc_sw128(sb + k * 2048, 8192, 1024), idesc, accum);
             if (kSwiGLU)
               mma_bf16_ss(d0 + 128, adesc, smem_desc_sw128(sb + 16384 + k * 2048, 8192, 1024),
@@ -192,7 +211,7 @@ __global__ void __launch_bounds__(GThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      const VarTile ti = var_tile(s.E, s_tp, s_mt, s_st, s_en, t);
+      const VarTile ti = var_tile(s.E, s_tp, s_mt, s_tn, s_st, s_en, t);
       bool got = !*abort_flag && mbar_wait(&sm->tmem_full[acc], acc_phase);
       if (!__all_sync(0xffffffffu, got)) { *abort_flag = 1; break; }
       tc_fence_after();
@@ -200,6 +219,30 @@ __global__ void __launch_bounds__(GThreads, 1)
       const int n_base = ti.n * kCols;
       const int row_base = ti.r0 + lg * 32;
       const int ncols = s.N[ti.e];
+      if (!kSwiGLU && s.ks[ti.e] > 1) {
+        // split tile: this thread's row of fp32 partial sums, 128 bytes per store run
+        const int grow = row_base + lane;
+        float* prow = s.partial + ((int64_t)ti.sp * s.prows + grow) * s.ldo;
+#pragma unroll 1
+        for (int c = 0; c < kCols; c += 32) {
+          uint32_t v[32];
+          tmem_ld32(t_row + c, v);
+          tmem_ld_wait();
+          const int col0 = n_base + c;
+          if (grow < ti.r_end && col0 < ncols) {
+            float4* dst = reinterpret_cast<float4*>(prow + col0);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              dst[i] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                   __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm->tmem_empty[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        continue;
+      }
       const uint32_t stage = smem_u32(epi_stage);
       constexpr int kBlocks = kCols / 64;
 #pragma unroll 1
@@ -274,9 +317,62 @@ __global__ void __launch_bounds__(GThreads, 1)
 // Launches one variable-extent grouped GEMM.  a: [rows, lda] bf16 (lda >=
 // every K_e); w0 (and w1 for SwiGLU): E host-side device pointers of
 // [K_e, N_e] bf16 weights; out [rows, ldo].
+// Sums the fp32 partials of the K-split experts in split order and stores
+// bf16; rows of unsplit experts were stored by the GEMM itself.  One warp
+// per row, 4 columns per lane per step.
+__global__ void k_var_reduce(const float* __restrict__ partial, int64_t prows, int64_t ldo,
+                             const int32_t* __restrict__ offsets, VarShape s, int64_t rows,
+                             uint16_t* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wpb = blockDim.x >> 5;
+  for (int64_t r = blockIdx.x * wpb + (threadIdx.x >> 5); r < rows;
+       r += (int64_t)gridDim.x * wpb) {
+    int e = 0;
+    while (e + 1 < s.E && offsets[e + 1] <= r) ++e;
+    const int ks = s.ks[e];
+    if (ks <= 1) continue;
+    for (int c = lane * 4; c < s.N[e]; c += 128) {
+      float4 acc = *reinterpret_cast<const float4*>(partial + r * ldo + c);
+      for (int sp = 1; sp < ks; ++sp) {
+        const float4 v = *reinterpret_cast<const float4*>(partial + (sp * prows + r) * ldo + c);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      uint2 o;
+      o.x = pack_bf16x2(acc.x, acc.y);
+      o.y = pack_bf16x2(acc.z, acc.w);
+      *reinterpret_cast<uint2*>(out + r * ldo + c) = o;
+    }
+  }
+}
+
+// K splits of expert e for the down GEMM of a small batch: with few rows the
+// grid would otherwise run each wide expert's long-K tiles on a few SMs.
+// Splits bring every expert's tiles near the shortest K; none when the rows
+// alone fill the GPU.  ks[e] = 1 means no split.
+inline int plan_splits(int64_t rows, const int64_t* K, int E, int* ks) {
+  int64_t kmin = K[0];
+  for (int e = 1; e < E; ++e) kmin = std::min(kmin, K[e]);
+  int kmax = 1;
+  for (int e = 0; e < E; ++e) {
+    ks[e] = 1;
+    if (rows <= kSplitRows && kmin > 0) {
+      const int64_t nkb = (K[e] + GBK - 1) / GBK;
+      const int64_t want = std::min<int64_t>(kMaxSplits, std::max<int64_t>(1, K[e] / kmin));
+      const int64_t per = (nkb + want - 1) / want;
+      ks[e] = (int)((nkb + per - 1) / per);  // every split gets at least one k block
+    }
+    kmax = std::max(kmax, ks[e]);
+  }
+  return kmax;
+}
+
 int var_launch(bool swiglu, const void* a, int64_t lda, const void* const* w0,
                const void* const* w1, void* out, int64_t ldo, const int32_t* offsets,
-               int64_t rows, const int64_t* K, const int64_t* N, int E, cudaStream_t st) {
+               int64_t rows, const int64_t* K, const int64_t* N, int E, cudaStream_t st,
+               float* partial = nullptr) {
   RB_CHECK_ARG(E >= 1 && E <= kVarMaxE, "grouped_gemm_var: E=%d unsupported (1..%d)", E,
                kVarMaxE);
   RB_CHECK_ARG(rows >= 0 && rows < (1ll << 31), "grouped_gemm_var: bad row count");
@@ -330,7 +426,14 @@ int var_launch(bool swiglu, const void* a, int64_t lda, const void* const* w0,
   sh.ldo = ldo;
   sh.offsets = offsets;
   sh.out = static_cast<uint16_t*>(out);
-  const int64_t max_tiles = (rows / GBM + E) * max_tn;
+  sh.partial = partial;
+  sh.prows = rows;
+  int max_ks = 1;
+  if (!swiglu && partial)
+    max_ks = plan_splits(rows, K, E, sh.ks);
+  else
+    for (int e = 0; e < E; ++e) sh.ks[e] = 1;
+  const int64_t max_tiles = (rows / GBM + E) * max_tn * max_ks;
   const int grid = (int)std::min<int64_t>(num_sms(), max_tiles);
   if (swiglu) {
     RB_CUDA(cudaFuncSetAttribute(k_grouped_var<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -340,6 +443,12 @@ int var_launch(bool swiglu, const void* a, int64_t lda, const void* const* w0,
     RB_CUDA(cudaFuncSetAttribute(k_grouped_var<false>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, GSmemBytes));
     k_grouped_var<false><<<grid, GThreads, GSmemBytes, st>>>(tA, maps, sh);
+    RB_LAUNCH_CHECK();
+    if (max_ks > 1) {
+      const int64_t want = (rows + 7) / 8;
+      k_var_reduce<<<(unsigned)std::min<int64_t>(want, (int64_t)num_sms() * 16), 256, 0, st>>>(
+          partial, rows, ldo, offsets, sh, rows, static_cast<uint16_t*>(out));
+    }
   }
   RB_LAUNCH_CHECK();
   return REMORA_B200_OK;
@@ -347,7 +456,7 @@ int var_launch(bool swiglu, const void* a, int64_t lda, const void* const* w0,
 
 struct HeteroWs {
   int32_t *idx, *counts, *offsets, *perm, *inv, *block_counts;
-  float* w;
+  float *w, *partial;
   uint16_t *xs, *h, *y;
   size_t bytes;
 };
@@ -371,6 +480,8 @@ inline HeteroWs hetero_ws(void* base, int64_t T, int64_t D, int64_t Fmax, int E,
   L.xs = reinterpret_cast<uint16_t*>(take(n * D * 2));
   L.h = reinterpret_cast<uint16_t*>(take(n * Fmax * 2));
   L.y = reinterpret_cast<uint16_t*>(take(n * D * 2));
+  // fp32 partial sums of the split down GEMM (small batches only)
+  L.partial = n <= kSplitRows ? reinterpret_cast<float*>(take(kMaxSplits * n * D * 4)) : nullptr;
   L.bytes = o;
   return L;
 }
@@ -454,7 +565,8 @@ extern "C" int remora_b200_moe_hetero_layer_bf16(const void* x, const void* wr,
     return rc;
   if ((rc = gather_launch(x, L.perm, n, k, D, L.xs, st))) return rc;
   if ((rc = var_launch(true, L.xs, D, wg, wu, L.h, ldh, L.offsets, n, K, F, E, st))) return rc;
-  if ((rc = var_launch(false, L.h, ldh, wd, nullptr, L.y, D, L.offsets, n, F, N, E, st)))
+  if ((rc = var_launch(false, L.h, ldh, wd, nullptr, L.y, D, L.offsets, n, F, N, E, st,
+                       L.partial)))
     return rc;
   return combine_launch(L.y, L.inv, L.w, T, k, D, out, st);
 }
