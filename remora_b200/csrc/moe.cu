@@ -20,8 +20,7 @@ namespace moe {
 // loop nest (linalg.fill + reduction, convert-linalg-to-loops), so the
 // top-k indices are bit-identical to it.  A bf16 x bf16 product is exact in
 // fp32, so fmaf(a, b, acc) == acc + a*b here.
-constexpr int kRouterDCh = 32;             // d per shared-memory chunk
-constexpr int kRowPadF = kRouterDCh + 4;   // padded f32 row (16-byte aligned rows)
+constexpr int kRouterDCh = 32;             // d per shared-memory chunk (default)
 
 __device__ __forceinline__ bool topk_before(float a, int ia, float b, int ib) {
   const bool an = a != a, bn = b != b;
@@ -46,21 +45,23 @@ __device__ __forceinline__ bool topk_before(float a, int ia, float b, int ib) {
 // busy) when there are few tokens and the register block RT x EPL is large.
 // Host contract: RT <= LE (so at most WARPS * 32 tokens per block),
 // E % 8 == 0 or E <= 128, k <= 16.
-template <int RT, int EPL, int WARPS>
+template <int RT, int EPL, int WARPS, int DCH = kRouterDCh>
 __global__ void __launch_bounds__(WARPS * 32)
     k_router_topk(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr, int T, int D,
                   int E, int k, int LE, int32_t* __restrict__ idx_out,
                   float* __restrict__ w_out) {
   extern __shared__ __align__(16) uint8_t sm_raw[];
   constexpr int kRouterThreads = WARPS * 32;
+  constexpr int kChunk = DCH;      // d per shared-memory chunk
+  constexpr int kPad = DCH + 4;    // padded f32 row (16-byte aligned rows)
   constexpr int kWarps = WARPS;
-  constexpr int kDC8 = kRouterDCh / 8;
+  constexpr int kDC8 = kChunk / 8;
   const int LT = 32 / LE;              // token groups per warp
   const int TGB = kWarps * LT;         // token groups per block
   const int TPB = TGB * RT;            // tokens per block
   const int EP = LE * EPL;             // staged router rows (>= E)
-  float* xs = reinterpret_cast<float*>(sm_raw);  // [TPB][kRowPadF]
-  float* ws = xs + TPB * kRowPadF;               // [EP][kRowPadF] (router chunk, transposed)
+  float* xs = reinterpret_cast<float*>(sm_raw);  // [TPB][kPad]
+  float* ws = xs + TPB * kPad;               // [EP][kPad] (router chunk, transposed)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tg = lane / LE, le = lane % LE;
   const int gtg = warp * LT + tg;      // token group within the block
@@ -71,7 +72,7 @@ __global__ void __launch_bounds__(WARPS * 32)
 #pragma unroll
     for (int j = 0; j < EPL; ++j) acc[r][j] = 0.0f;
   // rows beyond E stay zero (their experts are never selected)
-  for (int i = tid; i < (EP - E) * kRowPadF; i += kRouterThreads) ws[E * kRowPadF + i] = 0.0f;
+  for (int i = tid; i < (EP - E) * kPad; i += kRouterThreads) ws[E * kPad + i] = 0.0f;
 
   // Block token q = g*RT + r (token group g) lives in smem row r*TGB + g: the
   // LT token groups of a warp read LT adjacent rows for a given r.
@@ -80,15 +81,15 @@ __global__ void __launch_bounds__(WARPS * 32)
   // shared stores are conflict-free); otherwise single values.
   const bool vec_w = (E % 8) == 0;
   const int nx = TPB * kDC8;                              // x pieces of 8 per chunk
-  const int nw = vec_w ? kRouterDCh * (E / 8) : kRouterDCh * E;
+  const int nw = vec_w ? kChunk * (E / 8) : kChunk * E;
   // pieces per thread: TPB <= WARPS*32 (RT <= LE) and E <= 32*EPL (LE <= 32)
   constexpr int kXPT = kDC8;
-  constexpr int kWPT = (128 * EPL + kRouterThreads - 1) / kRouterThreads;   // 16-byte pieces
-  constexpr int kWPS = (1024 * EPL + kRouterThreads - 1) / kRouterThreads;  // single values
+  constexpr int kWPT = (4 * kChunk * EPL + kRouterThreads - 1) / kRouterThreads;   // 16-byte
+  constexpr int kWPS = (32 * kChunk * EPL + kRouterThreads - 1) / kRouterThreads;  // single
   uint4 xpre[kXPT];
   uint32_t wreg[4 * kWPT > kWPS ? 4 * kWPT : kWPS];
   auto load_chunk = [&](int d0) {
-    const int dc = min(kRouterDCh, D - d0);
+    const int dc = min(kChunk, D - d0);
 #pragma unroll
     for (int j = 0; j < kXPT; ++j) {
       const int i = tid + j * kRouterThreads;
@@ -101,7 +102,7 @@ __global__ void __launch_bounds__(WARPS * 32)
 #pragma unroll
       for (int j = 0; j < kWPT; ++j) {
         const int i = tid + j * kRouterThreads;
-        const int dd = i % kRouterDCh, e0 = (i / kRouterDCh) * 8;
+        const int dd = i % kChunk, e0 = (i / kChunk) * 8;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (i < nw && dd < dc) v = *reinterpret_cast<const uint4*>(wr + (int64_t)(d0 + dd) * E + e0);
         wreg[4 * j] = v.x;
@@ -113,7 +114,7 @@ __global__ void __launch_bounds__(WARPS * 32)
 #pragma unroll
       for (int j = 0; j < kWPS; ++j) {
         const int i = tid + j * kRouterThreads;
-        const int dd = i % kRouterDCh, e = i / kRouterDCh;
+        const int dd = i % kChunk, e = i / kChunk;
         wreg[j] = (i < nw && dd < dc) ? wr[(int64_t)(d0 + dd) * E + e] : 0u;
       }
     }
@@ -126,7 +127,7 @@ __global__ void __launch_bounds__(WARPS * 32)
       const int row = i / kDC8, c8 = (i % kDC8) * 8;
       const int srow = (row % RT) * TGB + row / RT;
       const uint4 v = xpre[j];
-      float4* dst = reinterpret_cast<float4*>(xs + srow * kRowPadF + c8);
+      float4* dst = reinterpret_cast<float4*>(xs + srow * kPad + c8);
       dst[0] = make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u),
                            __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
       dst[1] = make_float4(__uint_as_float(v.z << 16), __uint_as_float(v.z & 0xffff0000u),
@@ -137,11 +138,11 @@ __global__ void __launch_bounds__(WARPS * 32)
       for (int j = 0; j < kWPT; ++j) {
         const int i = tid + j * kRouterThreads;
         if (i >= nw) break;
-        float* col = ws + (i / kRouterDCh) * 8 * kRowPadF + i % kRouterDCh;
+        float* col = ws + (i / kChunk) * 8 * kPad + i % kChunk;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          col[(2 * q) * kRowPadF] = __uint_as_float(wreg[4 * j + q] << 16);
-          col[(2 * q + 1) * kRowPadF] = __uint_as_float(wreg[4 * j + q] & 0xffff0000u);
+          col[(2 * q) * kPad] = __uint_as_float(wreg[4 * j + q] << 16);
+          col[(2 * q + 1) * kPad] = __uint_as_float(wreg[4 * j + q] & 0xffff0000u);
         }
       }
     } else {
@@ -149,27 +150,27 @@ __global__ void __launch_bounds__(WARPS * 32)
       for (int j = 0; j < kWPS; ++j) {
         const int i = tid + j * kRouterThreads;
         if (i >= nw) break;
-        ws[(i / kRouterDCh) * kRowPadF + i % kRouterDCh] = __uint_as_float(wreg[j] << 16);
+        ws[(i / kChunk) * kPad + i % kChunk] = __uint_as_float(wreg[j] << 16);
       }
     }
   };
 
-  const float* wrow = ws + le * kRowPadF;
-  const float* xrow = xs + gtg * kRowPadF;
+  const float* wrow = ws + le * kPad;
+  const float* xrow = xs + gtg * kPad;
   load_chunk(0);
-  for (int d0 = 0; d0 < D; d0 += kRouterDCh) {
+  for (int d0 = 0; d0 < D; d0 += kChunk) {
     store_chunk();
     __syncthreads();
-    if (d0 + kRouterDCh < D) load_chunk(d0 + kRouterDCh);
+    if (d0 + kChunk < D) load_chunk(d0 + kChunk);
 #pragma unroll 2
-    for (int dd = 0; dd < kRouterDCh; dd += 4) {
+    for (int dd = 0; dd < kChunk; dd += 4) {
       float4 wv[EPL];
 #pragma unroll
       for (int j = 0; j < EPL; ++j)
-        wv[j] = *reinterpret_cast<const float4*>(wrow + j * LE * kRowPadF + dd);
+        wv[j] = *reinterpret_cast<const float4*>(wrow + j * LE * kPad + dd);
 #pragma unroll
       for (int r = 0; r < RT; ++r) {
-        const float4 xv = *reinterpret_cast<const float4*>(xrow + r * TGB * kRowPadF + dd);
+        const float4 xv = *reinterpret_cast<const float4*>(xrow + r * TGB * kPad + dd);
 #pragma unroll
         for (int j = 0; j < EPL; ++j) {
           acc[r][j] = fmaf(xv.x, wv[j].x, acc[r][j]);

@@ -318,33 +318,39 @@ __global__ void __launch_bounds__(GThreads, 1)
 // every K_e); w0 (and w1 for SwiGLU): E host-side device pointers of
 // [K_e, N_e] bf16 weights; out [rows, ldo].
 // Sums the fp32 partials of the K-split experts in split order and stores
-// bf16; rows of unsplit experts were stored by the GEMM itself.  One warp
-// per row, 4 columns per lane per step.
+// bf16; rows of unsplit experts were stored by the GEMM itself.  One thread
+// per 4 columns of a row, all of its splits' loads issued before the sum.
 __global__ void k_var_reduce(const float* __restrict__ partial, int64_t prows, int64_t ldo,
                              const int32_t* __restrict__ offsets, VarShape s, int64_t rows,
                              uint16_t* __restrict__ out) {
-  const int lane = threadIdx.x & 31;
-  const int64_t wpb = blockDim.x >> 5;
-  for (int64_t r = blockIdx.x * wpb + (threadIdx.x >> 5); r < rows;
-       r += (int64_t)gridDim.x * wpb) {
+  __shared__ int off[kVarMaxE + 1];
+  if (threadIdx.x <= s.E) off[threadIdx.x] = offsets[threadIdx.x];
+  __syncthreads();
+  const int64_t groups = ldo / 4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * groups;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / groups, c = (i - r * groups) * 4;
     int e = 0;
-    while (e + 1 < s.E && offsets[e + 1] <= r) ++e;
+    while (e + 1 < s.E && off[e + 1] <= r) ++e;
     const int ks = s.ks[e];
-    if (ks <= 1) continue;
-    for (int c = lane * 4; c < s.N[e]; c += 128) {
-      float4 acc = *reinterpret_cast<const float4*>(partial + r * ldo + c);
-      for (int sp = 1; sp < ks; ++sp) {
-        const float4 v = *reinterpret_cast<const float4*>(partial + (sp * prows + r) * ldo + c);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+    if (ks <= 1 || c >= s.N[e]) continue;
+    float4 v[kMaxSplits];
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; ++sp)
+      if (sp < ks) v[sp] = *reinterpret_cast<const float4*>(partial + (sp * prows + r) * ldo + c);
+    float4 acc = v[0];
+#pragma unroll
+    for (int sp = 1; sp < kMaxSplits; ++sp)
+      if (sp < ks) {
+        acc.x += v[sp].x;
+        acc.y += v[sp].y;
+        acc.z += v[sp].z;
+        acc.w += v[sp].w;
       }
-      uint2 o;
-      o.x = pack_bf16x2(acc.x, acc.y);
-      o.y = pack_bf16x2(acc.z, acc.w);
-      *reinterpret_cast<uint2*>(out + r * ldo + c) = o;
-    }
+    uint2 o;
+    o.x = pack_bf16x2(acc.x, acc.y);
+    o.y = pack_bf16x2(acc.z, acc.w);
+    *reinterpret_cast<uint2*>(out + r * ldo + c) = o;
   }
 }
 
@@ -445,8 +451,9 @@ int var_launch(bool swiglu, const void* a, int64_t lda, const void* const* w0,
     k_grouped_var<false><<<grid, GThreads, GSmemBytes, st>>>(tA, maps, sh);
     RB_LAUNCH_CHECK();
     if (max_ks > 1) {
-      const int64_t want = (rows + 7) / 8;
-      k_var_reduce<<<(unsigned)std::min<int64_t>(want, (int64_t)num_sms() * 16), 256, 0, st>>>(
+      RB_CHECK_ARG(ldo % 4 == 0, "grouped_gemm_var: split output stride must be a multiple of 4");
+      const int64_t want = (rows * (ldo / 4) + 255) / 256;
+      k_var_reduce<<<(unsigned)std::min<int64_t>(want, (int64_t)num_sms() * 8), 256, 0, st>>>(
           partial, rows, ldo, offsets, sh, rows, static_cast<uint16_t*>(out));
     }
   }

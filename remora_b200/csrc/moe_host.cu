@@ -12,7 +12,7 @@ inline int64_t dispatch_blocks(int64_t n) { return (n + kDispThreads - 1) / kDis
 // Router tile: lanes per token group LE, experts per lane EPL, tokens per
 // lane RT, warps per block, and the launch geometry that follows.
 struct RouterPlan {
-  int le, epl, rt, warps;
+  int le, epl, rt, warps, dch;
   int64_t tpb, grid;
   size_t smem;
 };
@@ -28,7 +28,9 @@ RouterPlan router_plan(int64_t T, int E) {
   // per block found nothing faster for 64 experts (LE 32 with EPL 2 and RT
   // 16, the largest register block, is 1.4-2x slower).  With 5-8 experts
   // (LE 8, EPL 1) blocks of 2 warps with RT 2 are fastest: (8192, 4096, 8)
-  // 84 us against 104 us with 8-warp blocks.
+  // 84 us against 104 us with 8-warp blocks.  With few tokens the grid is
+  // small and each 32-d chunk costs about one global-load latency, so up to
+  // 2048 tokens the chunks are 128 d long (4x fewer round trips).
   int epl = 1, le = 1;
   if (E > 128) {
     epl = 8;
@@ -60,8 +62,9 @@ RouterPlan router_plan(int64_t T, int E) {
   p.epl = epl;
   p.rt = rt;
   p.warps = warps;
+  p.dch = (warps == 2 && T <= 2048) ? 128 : kRouterDCh;
   p.tpb = tokens_per_block(rt);
-  p.smem = (size_t)(p.tpb + le * epl) * kRowPadF * 4;
+  p.smem = (size_t)(p.tpb + le * epl) * (p.dch + 4) * 4;
   p.grid = (T + p.tpb - 1) / p.tpb;
   return p;
 }
@@ -90,7 +93,8 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
     return REMORA_B200_OK;
   };
   int rc;
-  switch (warps == 2 ? -1 : epl * 100 + rt) {
+  switch (warps == 2 ? (pl.dch == 128 ? -2 : -1) : epl * 100 + rt) {
+    case -2: rc = launch(k_router_topk<2, 1, 2, 128>); break;
     case -1: rc = launch(k_router_topk<2, 1, 2>); break;
     case 101: rc = launch(k_router_topk<1, 1, 8>); break;
     case 102: rc = launch(k_router_topk<2, 1, 8>); break;
