@@ -28,9 +28,11 @@ RouterPlan router_plan(int64_t T, int E) {
   // per block found nothing faster for 64 experts (LE 32 with EPL 2 and RT
   // 16, the largest register block, is 1.4-2x slower).  With 5-8 experts
   // (LE 8, EPL 1) blocks of 2 warps with RT 2 are fastest: (8192, 4096, 8)
-  // 84 us against 104 us with 8-warp blocks.  With few tokens the grid is
-  // small and each 32-d chunk costs about one global-load latency, so up to
-  // 2048 tokens the chunks are 128 d long (4x fewer round trips).
+  // 84 us against 104 us with 8-warp blocks.  With few blocks each 32-d
+  // chunk costs about one global-load latency, so the latency-bound shapes
+  // take 64-d chunks: (8192, 4096, 8) 68 us, (512, 4096, 8) 56 us (86 us with
+  // 32-d chunks), (8192, 2048, 64) 126 us; with many tokens 32-d chunks stay
+  // best ((65536, 2048, 64): 660 us against 826 us with 64-d chunks).
   int epl = 1, le = 1;
   if (E > 128) {
     epl = 8;
@@ -47,8 +49,13 @@ RouterPlan router_plan(int64_t T, int E) {
   const int warps = (le == 8 && epl == 1) ? 2 : 8;
   auto tokens_per_block = [&](int rt) { return (int64_t)warps * (32 / le) * rt; };
   int rt = 1;
+  int dch = kRouterDCh;
   if (warps == 2) {
     rt = 2;
+    dch = 64;
+  } else if (le == 16 && epl == 4) {  // 33-64 experts: swept at 8192 to 65536 tokens
+    rt = T > 16384 ? 8 : 4;
+    dch = T <= 8192 ? 64 : kRouterDCh;
   } else {
     for (int c = 16; c > 1; c /= 2)
       if (c <= le && c * epl <= 32 &&
@@ -62,7 +69,7 @@ RouterPlan router_plan(int64_t T, int E) {
   p.epl = epl;
   p.rt = rt;
   p.warps = warps;
-  p.dch = (warps == 2 && T <= 2048) ? 128 : kRouterDCh;
+  p.dch = dch;
   p.tpb = tokens_per_block(rt);
   p.smem = (size_t)(p.tpb + le * epl) * (p.dch + 4) * 4;
   p.grid = (T + p.tpb - 1) / p.tpb;
@@ -93,9 +100,9 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
     return REMORA_B200_OK;
   };
   int rc;
-  switch (warps == 2 ? (pl.dch == 128 ? -2 : -1) : epl * 100 + rt) {
-    case -2: rc = launch(k_router_topk<2, 1, 2, 128>); break;
-    case -1: rc = launch(k_router_topk<2, 1, 2>); break;
+  switch (warps == 2 ? -1 : (pl.dch == 64 ? -2 : epl * 100 + rt)) {
+    case -1: rc = launch(k_router_topk<2, 1, 2, 64>); break;
+    case -2: rc = launch(k_router_topk<4, 4, 8, 64>); break;
     case 101: rc = launch(k_router_topk<1, 1, 8>); break;
     case 102: rc = launch(k_router_topk<2, 1, 8>); break;
     case 104: rc = launch(k_router_topk<4, 1, 8>); break;
