@@ -46,7 +46,7 @@ struct Params {
 struct Smem {
   uint64_t q_full;
   uint64_t k_full[2], v_full[2], kv_empty[2];
-  uint64_t s_full[2], p_full[2];
+  uint64_t s_full[2], p_half[2], p_full[2];  // P columns 0-63 stored (and O rescaled) / all
   uint64_t o_final;
   uint32_t tmem_base;
   int abort_flag;
@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&sm->v_full[i], 1);
       mbar_init(&sm->kv_empty[i], 1);
       mbar_init(&sm->s_full[i], 1);
+      mbar_init(&sm->p_half[i], 4);
       mbar_init(&sm->p_full[i], 4);
     }
     mbar_init(&sm->o_final, 1);
@@ -152,12 +153,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(&sm->s_full[w]);
       };
-      auto issue_pv = [&](int w, int st, bool first) {
+      // P V in two halves of K: keys 0-63 once the softmax has stored that half of
+      // P (p_half), keys 64-127 once it has stored the rest (p_full)
+      auto issue_pv = [&](int w, int st, bool first, int k0) {
 #pragma unroll
-        for (int k = 0; k < BKV / 16; ++k)
+        for (int k = k0; k < k0 + BKV / 32; ++k)
           mma_bf16_ts(tbase + 256 + w * HD, tbase + w * BKV + k * 8,
                       smem_desc_sw128(sv + st * kTileBytes + k * 2048, kHalf, 1024), id_pv,
                       (!first || k > 0) ? 1u : 0u);
+      };
+      auto pv = [&](int w, int st, int j) -> bool {
+        if (!mbar_wait(&sm->p_half[w], j & 1)) return false;
+        tc_fence_after();
+        issue_pv(w, st, j == 0, 0);
+        if (!mbar_wait(&sm->p_full[w], j & 1)) return false;
+        tc_fence_after();
+        issue_pv(w, st, j == 0, BKV / 32);
+        return true;
       };
       bool ok = mbar_wait(&sm->q_full, 0) && mbar_wait(&sm->k_full[0], 0);
       if (ok) {
@@ -170,18 +182,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t phn = ((j + 1) >> 1) & 1;
         if (!mbar_wait(&sm->v_full[st], (j >> 1) & 1)) { ok = false; break; }
         if (j < n0) {
-          if (!mbar_wait(&sm->p_full[0], j & 1)) { ok = false; break; }
-          tc_fence_after();
-          issue_pv(0, st, j == 0);
+          if (!pv(0, st, j)) { ok = false; break; }
           if (j + 1 < n0) {
             if (!mbar_wait(&sm->k_full[stn], phn)) { ok = false; break; }
             tc_fence_after();
             issue_s(0, stn);
           }
         }
-        if (!mbar_wait(&sm->p_full[1], j & 1)) { ok = false; break; }
-        tc_fence_after();
-        issue_pv(1, st, j == 0);
+        if (!pv(1, st, j)) { ok = false; break; }
         mma_commit(&sm->kv_empty[st]);
         if (j + 1 < n1) {
           if (!mbar_wait(&sm->k_full[stn], phn)) { ok = false; break; }
@@ -247,24 +255,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float mu = (m == -INFINITY) ? 0.0f : m;
       // P packs two bf16 per 32-bit column (even element in the low half);
-      // r[c/2] is written only after r[c] and r[c+1] have been read.
+      // r[c/2] is written only after r[c] and r[c+1] have been read.  P goes to
+      // TMEM in two halves so that the P V MMA starts on keys 0-63 while the
+      // exponentials of keys 64-127 run.
       float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 partial row sums
 #pragma unroll
-      for (int c = 0; c < BKV; c += 2) {
+      for (int c = 0; c < BKV / 2; c += 2) {
         const float a = ex2(fmaf(__uint_as_float(r[c]), p.sl2, -mu));
         const float b = ex2(fmaf(__uint_as_float(r[c + 1]), p.sl2, -mu));
         ps[(c >> 1) & 7] += a + b;
         r[c >> 1] = pack_bf16x2(a, b);
       }
-      l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
+      for (int c = 0; c < 2; ++c)
         tmem_st16(t_s + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&r[c * 16]));
       if (__any_sync(0xffffffffu, rescale_o)) {
         // O holds the products of earlier tiles: PV of tile j-1 was issued
         // before S of tile j, so it has completed once s_full fired; PV of
-        // tile j waits for p_full below.  Done after P is written, when the
-        // S registers are free.
+        // tile j waits for p_half below.  Done after the first half of P is
+        // written, when half of the S registers are free.
         const float f = rescale_o ? alpha : 1.0f;
 #pragma unroll 1
         for (int c = 0; c < HD; c += 32) {
@@ -281,6 +290,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st16(t_o + c + 16, hi);
         }
       }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sm->p_half[w]);
+#pragma unroll
+      for (int c = BKV / 2; c < BKV; c += 2) {
+        const float a = ex2(fmaf(__uint_as_float(r[c]), p.sl2, -mu));
+        const float b = ex2(fmaf(__uint_as_float(r[c + 1]), p.sl2, -mu));
+        ps[(c >> 1) & 7] += a + b;
+        r[c >> 1] = pack_bf16x2(a, b);
+      }
+      l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+#pragma unroll
+      for (int c = 2; c < 4; ++c)
+        tmem_st16(t_s + c * 16, *reinterpret_cast<const uint32_t(*)[16]>(&r[c * 16]));
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
