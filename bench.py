@@ -56,6 +56,9 @@ NCU_TRAFFIC_BYTES = {
     # one-rank capture of the merged expert kernel at the per-rank shape of the 8-GPU
     # layer (65536 rows): profiles/moe_ep_experts_p1_8x65536_full.md
     "moe_ep_experts": 1321200000,
+    # [2,16,4096,128] capture (155.2 MB) scaled by 4 to the [4,32,4096,128] launch:
+    # profiles/attention_causal_2x16x4096_full.md
+    "attention": 620900352,
 }
 
 MOE_CONFIGS = {
