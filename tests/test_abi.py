@@ -87,3 +87,40 @@ def test_expert_parallel_entry_points_validate_before_cuda():
     assert rc == rb.ERR_INVALID                                              # rank >= P
     rc = L.remora_b200_moe_ep_barrier(p, null, P, 0, 1, None)
     assert rc == rb.ERR_INVALID
+
+
+def test_heterogeneous_and_nccl_entry_points_validate_without_gpu():
+    """The heterogeneous-layer, NCCL expert-parallel and peer-buffer entry
+    points reject bad arguments on the host, before any CUDA or NCCL call."""
+    import remora_b200 as rb
+
+    L = rb.lib()
+    F = (ctypes.c_int64 * 8)(14336, 14336, 8192, 8192, 4096, 4096, 2048, 2048)
+    assert L.remora_b200_moe_hetero_workspace_bytes(512, 4096, F, 8, 1) > 0
+    assert L.remora_b200_moe_hetero_workspace_bytes(512, 4096, F, 17, 1) == 0   # E > 16
+    assert L.remora_b200_moe_hetero_workspace_bytes(512, 4096, F, 8, 9) == 0    # k > E
+    assert L.remora_b200_moe_hetero_workspace_bytes(512, 4096, None, 8, 1) == 0
+    buf = ctypes.create_string_buffer(4096)
+    p = ctypes.addressof(buf)
+    ptrs = (ctypes.c_void_p * 8)(*([p] * 8))
+    bad = (ctypes.c_int64 * 8)(14336, 96, 8192, 8192, 4096, 4096, 2048, 2048)  # 96 % 64 != 0
+    rc = L.remora_b200_moe_hetero_layer_bf16(p, p, ptrs, ptrs, ptrs, bad, p, 512, 4096, 8, 1, p,
+                                             1 << 30, None)
+    assert rc == rb.ERR_INVALID and "F[1]" in rb.last_error()
+    rc = L.remora_b200_moe_hetero_layer_bf16(p, p, ptrs, ptrs, ptrs, F, p, 512, 4040, 8, 1, p,
+                                             1 << 30, None)
+    assert rc == rb.ERR_INVALID                                                # D % 32
+    rc = L.remora_b200_moe_hetero_layer_bf16(p, p, ptrs, ptrs, ptrs, F, p, 512, 4096, 8, 1, p,
+                                             16, None)
+    assert rc == rb.ERR_INVALID and "workspace" in rb.last_error()
+    # NCCL expert parallelism: a null communicator is rejected before NCCL is used
+    rc = L.remora_b200_moe_ep_nccl_bf16(p, p, p, p, p, p, 512, 4096, 14336, 8, 2, None, 1000, p,
+                                        1 << 30, None)
+    assert rc in (rb.ERR_INVALID, rb.ERR_NCCL)
+    assert L.remora_b200_moe_ep_nccl_workspace_bytes(1 << 40, 2048, 1536, 64, 8, 8) == 0
+    # peer buffers: null arguments
+    out = ctypes.c_void_p()
+    assert L.remora_b200_peer_alloc(0, ctypes.byref(out), p) == rb.ERR_INVALID
+    assert L.remora_b200_peer_open(None, ctypes.byref(out)) == rb.ERR_INVALID
+    assert L.remora_b200_peer_close(None) == rb.ERR_INVALID
+    assert L.remora_b200_peer_free(None) == rb.OK
