@@ -242,6 +242,8 @@ def attention_rows(q: np.ndarray, k: np.ndarray, v: np.ndarray, rows: np.ndarray
 def router_topk(x: np.ndarray, wr: np.ndarray, k: int, return_logits: bool = False):
     """M1: logits (increasing-d fp32), top-k indices, softmax weights."""
     T, D = x.shape
+    if wr.ndim != 2 or wr.shape[0] != D or not 0 < k <= wr.shape[1]:
+        raise ValueError(f"router_topk: x {x.shape}, wr {wr.shape}, k {k} do not match")
     E = wr.shape[1]
     idx = np.empty((T, k), np.int32)
     w = np.empty((T, k), np.float32)

@@ -111,8 +111,8 @@ def test_attention_matches_dense_float64(orc):
 
 def test_topk_tie_and_nan_rules(orc):
     # ties -> lower index; NaN ranks above every number
-    x = np.array([[1.0, 0.0, 0.0, 0.0]], np.float32)
-    wr = np.array([[0.5, 2.0, 2.0, 0.5]], np.float32).reshape(1, 4)
+    x = np.array([[1.0]], np.float32)  # D = 1, so the logits are wr's row
+    wr = np.array([[0.5, 2.0, 2.0, 0.5]], np.float32)
     idx, _ = orc.router_topk(x, wr, 3)
     assert idx.tolist() == [[1, 2, 0]]
     wr2 = np.array([[0.5, np.nan, 2.0, 0.5]], np.float32).reshape(1, 4)
