@@ -223,6 +223,18 @@ int remora_b200_grouped_gemm_swiglu_bf16(const void* xs, const void* wg, const v
                                          const int32_t* offsets, int64_t rows, int64_t D,
                                          int64_t F, int E, void* stream);
 
+/* The SwiGLU grouped GEMM reading its rows straight from the tokens: row r
+ * of the problem is x[perm[r] / k] (perm from remora_b200_moe_dispatch), so
+ * the dispatched copy xs of the dispatch (mixtral_moe_layer.mlir:28-31) is
+ * never written; the GEMM's producer warp copies each A tile's rows from x
+ * into the swizzled shared-memory stage with cp.async.  x bf16
+ * [T, D]; perm int32 [rows = T*k]; otherwise as above.  h is identical to
+ * remora_b200_grouped_gemm_swiglu_bf16 on the gathered rows. */
+int remora_b200_grouped_gemm_swiglu_gather_bf16(const void* x, const int32_t* perm, int64_t T,
+                                                int k, const void* wg, const void* wu, void* h,
+                                                const int32_t* offsets, int64_t rows, int64_t D,
+                                                int64_t F, int E, void* stream);
+
 /* Grouped expert GEMM (the down projection, mixtral_moe_layer.mlir:42):
  * y[r, :] = a[r] . w[e] for the rows of expert e.  a bf16 [rows, K],
  * w bf16 [E, K, N], y bf16 [rows, N]; K % 8 == 0, N % 32 == 0. */

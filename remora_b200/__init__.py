@@ -76,6 +76,8 @@ _SIGNATURES = {
     "remora_b200_moe_dispatch_noalloc": ([P, I64, I, I, P, P, P, P, P], I),
     "remora_b200_moe_gather": ([P, P, I64, I, I64, P, P], I),
     "remora_b200_grouped_gemm_swiglu_bf16": ([P, P, P, P, P, I64, I64, I64, I, P], I),
+    "remora_b200_grouped_gemm_swiglu_gather_bf16": ([P, P, I64, I, P, P, P, P, I64, I64, I64, I,
+                                                     P], I),
     "remora_b200_grouped_gemm_bf16": ([P, P, P, P, I64, I64, I64, I, P], I),
     "remora_b200_grouped_gemm_swiglu_segments_bf16": ([P, P, P, P, P, P, I, I64, I64, I64, I, P],
                                                       I),
@@ -340,6 +342,24 @@ def grouped_gemm_swiglu(xs: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor,
     _check(lib().remora_b200_grouped_gemm_swiglu_bf16(
         xs.contiguous().data_ptr(), wg.contiguous().data_ptr(), wu.contiguous().data_ptr(),
         h.data_ptr(), offsets.data_ptr(), rows, D, F, E, _stream(xs)))
+    return h
+
+
+def grouped_gemm_swiglu_gather(x: torch.Tensor, perm: torch.Tensor, k: int, wg: torch.Tensor,
+                               wu: torch.Tensor, offsets: torch.Tensor,
+                               out: torch.Tensor | None = None) -> torch.Tensor:
+    """h = silu(x[perm // k] . wg[e]) * (x[perm // k] . wu[e]) over each expert's
+    row segment, the rows read from x by the GEMM itself (no gathered copy)."""
+    _dev(x, perm, wg, wu, offsets)
+    _bf16(x, wg, wu)
+    _i32(perm, offsets)
+    T, D = x.shape
+    rows = perm.numel()
+    E, _, F = wg.shape
+    h = torch.empty((rows, F), dtype=torch.bfloat16, device=x.device) if out is None else out
+    _check(lib().remora_b200_grouped_gemm_swiglu_gather_bf16(
+        x.contiguous().data_ptr(), perm.data_ptr(), T, k, wg.contiguous().data_ptr(),
+        wu.contiguous().data_ptr(), h.data_ptr(), offsets.data_ptr(), rows, D, F, E, _stream(x)))
     return h
 
 

@@ -232,6 +232,219 @@ __global__ void __launch_bounds__(WARPS * 32)
   }
 }
 
+// Router, bf16-ring form (E % 8 == 0, E <= LE * EPL).  Same arithmetic as
+// k_router_topk (one serial fp32 chain per (token, expert), increasing d,
+// from +0.0), different data movement and issue:
+//   * bf16 tiles of x ([TPB tokens][C d]) and of the router ([C d][E]) stream
+//     through an S-stage shared-memory ring by cp.async, S-1 chunks in flight
+//     ahead of the one being multiplied (one __syncthreads per chunk);
+//   * operands stay bf16 in shared memory (a 16-byte read carries 8 d of a
+//     token, an 8-byte read 4 experts of one d) and are widened to f32 in
+//     registers (a bf16 is the high half of its f32);
+//   * two adjacent experts of a token advance together with one
+//     fma.rn.f32x2 (two independent fmaf's, each rounded once: the chains are
+//     the same as with scalar fmaf);
+//   * the operands of the next 8-d step are read before the current step's
+//     FMAs are issued.
+// Shared-memory bandwidth to the registers, not the FMA pipe, bounds the
+// f32-staged forms: a 16-byte shared read costs four wavefronts for a warp
+// even when its lanes share addresses, so halving the bytes per operand
+// (bf16) and the FMA instructions (f32x2) is what moves the kernel.
+// Lane (token group tg of LE lanes, le) owns RT tokens (block rows
+// r*TGB + gtg) and the EPL experts e = g*4*LE + 4*le + jj (g < EPL/4,
+// jj < 4).  Router columns E..EP-1 are zero and never selected; rows past T
+// and d past D are zero-filled by cp.async (a +0.0 product leaves a chain
+// unchanged: no chain is ever -0.0).  Measured on B200 against
+// k_router_topk, indices and weights bit-identical: (65536, 2048, 64)
+// 660 -> 471 us; (8192, 2048, 64) 126 -> 105 us; (1000, 2056, 64) 127 ->
+// 50 us; (8192, 4096, 8) 68 -> 49 us; (512, 4096, 8) 56 -> 47 us.
+// {d0, d1} = fma.rn({a, a}, {b0, b1}, {d0, d1}): two fmaf's in one instruction.
+__device__ __forceinline__ void fma2_bcast(float& d0, float& d1, float a, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+      "mov.b64 ra, {%2, %2};\n\t"
+      "mov.b64 rb, {%3, %4};\n\t"
+      "mov.b64 rc, {%0, %1};\n\t"
+      "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rc;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a), "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+template <int LE, int EPL, int RT, int WARPS, int C, int S>
+struct RouterRing {
+  static constexpr int kThreads = WARPS * 32;
+  static constexpr int LT = 32 / LE;          // token groups per warp
+  static constexpr int TGB = WARPS * LT;      // token groups per block
+  static constexpr int TPB = TGB * RT;        // tokens per block
+  static constexpr int EP = LE * EPL;         // router columns covered (>= E)
+  static constexpr int XP = C + 8;            // bf16 token-row pitch (16-byte rows)
+  static constexpr int WP = EP + 8;           // bf16 router-row pitch
+  static constexpr int C8 = C / 8;
+  static constexpr int kStage = TPB * XP + C * WP;  // bf16 elements per ring stage
+  static constexpr size_t smem_bytes() { return (size_t)S * kStage * 2; }
+  static_assert(EPL % 4 == 0 && C % 16 == 0 && S >= 2 && 32 % LE == 0, "router ring shape");
+};
+
+template <int LE, int EPL, int RT, int WARPS, int C, int S>
+__global__ void __launch_bounds__(WARPS * 32)
+    k_router_ring(const uint16_t* __restrict__ x, const uint16_t* __restrict__ wr, int T, int D,
+                  int E, int k, int32_t* __restrict__ idx_out, float* __restrict__ w_out) {
+  using P = RouterRing<LE, EPL, RT, WARPS, C, S>;
+  constexpr int NT = P::kThreads, TGB = P::TGB, TPB = P::TPB, EP = P::EP, XP = P::XP,
+                WP = P::WP, C8 = P::C8, LT = P::LT, G = EPL / 4;
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  uint16_t* ring = reinterpret_cast<uint16_t*>(sm_raw);  // [S][TPB*XP + C*WP]
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tg = lane / LE, le = lane % LE;
+  const int gtg = warp * LT + tg;
+  const int t0 = blockIdx.x * TPB;
+  const int E8 = E / 8;
+  const int nch = (D + C - 1) / C;
+
+  // router columns E..EP-1 of every stage stay zero (the copies never write them)
+  for (int i = tid; i < S * C * (EP - E); i += NT) {
+    const int st = i / (C * (EP - E)), r = i % (C * (EP - E));
+    ring[st * P::kStage + TPB * XP + (r / (EP - E)) * WP + E + r % (EP - E)] = 0;
+  }
+  auto issue = [&](int c) {  // chunk c into ring stage c % S (one commit group)
+    if (c < nch) {
+      const int d0 = c * C;
+      uint16_t* rx = ring + (c % S) * P::kStage;
+      uint16_t* rw = rx + TPB * XP;
+#pragma unroll
+      for (int j = 0; j < (TPB * C8 + NT - 1) / NT; ++j) {
+        const int p = tid + j * NT;
+        if ((TPB * C8) % NT != 0 && p >= TPB * C8) break;
+        const int row = p / C8, c8 = (p % C8) * 8;
+        const bool ok = t0 + row < T && d0 + c8 < D;
+        cp_async16(rx + row * XP + c8, ok ? x + (int64_t)(t0 + row) * D + d0 + c8 : x, ok);
+      }
+      for (int p = tid; p < C * E8; p += NT) {
+        const int dd = p / E8, e8 = (p % E8) * 8;
+        const bool ok = d0 + dd < D;
+        cp_async16(rw + dd * WP + e8, ok ? wr + (int64_t)(d0 + dd) * E + e8 : wr, ok);
+      }
+    }
+    cp_async_commit();
+  };
+
+  float acc[RT][EPL];
+#pragma unroll
+  for (int r = 0; r < RT; ++r)
+#pragma unroll
+    for (int j = 0; j < EPL; ++j) acc[r][j] = 0.0f;
+
+#pragma unroll 1
+  for (int c = 0; c < S - 1; ++c) issue(c);
+#pragma unroll 1
+  for (int c = 0; c < nch; ++c) {
+    cp_async_wait<S - 2>();  // chunk c landed (this thread's copies) ...
+    __syncthreads();         // ... and everyone's; chunk c-1's stage is free again
+    issue(c + S - 1);
+    const uint16_t* bx = ring + (c % S) * P::kStage + gtg * XP;
+    const uint16_t* bw = ring + (c % S) * P::kStage + TPB * XP + 4 * le;
+    // operands of 8 d: RT token pieces (8 bf16 each) and, per d, G groups
+    // of 4 adjacent experts (4 bf16 each)
+    auto load = [&](uint4 (&xv)[RT], uint2 (&wv)[8][G], int dd) {
+#pragma unroll
+      for (int r = 0; r < RT; ++r)
+        xv[r] = *reinterpret_cast<const uint4*>(bx + r * TGB * XP + dd);
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+          wv[q][g] = *reinterpret_cast<const uint2*>(bw + (dd + q) * WP + g * 4 * LE);
+    };
+    auto mac = [&](const uint4 (&xv)[RT], const uint2 (&wv)[8][G]) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {  // d = dd + q, in increasing order
+        float wq[G][4];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          wq[g][0] = bf16_lo(wv[q][g].x);
+          wq[g][1] = bf16_hi(wv[q][g].x);
+          wq[g][2] = bf16_lo(wv[q][g].y);
+          wq[g][3] = bf16_hi(wv[q][g].y);
+        }
+#pragma unroll
+        for (int r = 0; r < RT; ++r) {
+          const uint32_t pair = (q >> 1) == 0 ? xv[r].x
+                                : (q >> 1) == 1 ? xv[r].y
+                                : (q >> 1) == 2 ? xv[r].z
+                                                : xv[r].w;
+          const float xq = (q & 1) ? bf16_hi(pair) : bf16_lo(pair);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            fma2_bcast(acc[r][4 * g + 0], acc[r][4 * g + 1], xq, wq[g][0], wq[g][1]);
+            fma2_bcast(acc[r][4 * g + 2], acc[r][4 * g + 3], xq, wq[g][2], wq[g][3]);
+          }
+        }
+      }
+    };
+    uint4 xa[RT], xb[RT];
+    uint2 wa[8][G], wb[8][G];
+    load(xa, wa, 0);
+#pragma unroll 1
+    for (int dd = 0; dd < C; dd += 16) {
+      load(xb, wb, dd + 8);
+      mac(xa, wa);
+      if (dd + 16 < C) load(xa, wa, dd + 16);
+      mac(xb, wb);
+    }
+  }
+  cp_async_wait<0>();
+
+  // top-k per token over the LE lanes of its group (EPL candidates per lane)
+  auto expert_of = [&](int j) { return (j >> 2) * 4 * LE + 4 * le + (j & 3); };
+#pragma unroll
+  for (int r = 0; r < RT; ++r) {
+    const int t = t0 + r * TGB + gtg;
+    uint32_t used = 0;
+#pragma unroll
+    for (int j = 0; j < EPL; ++j)
+      if (expert_of(j) >= E) used |= 1u << j;
+    float sel_v[16];
+    int sel_i[16];
+    for (int s = 0; s < k; ++s) {
+      float bv = 0.0f;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int j = 0; j < EPL; ++j)
+        if (!(used >> j & 1u) &&
+            (bi == 0x7fffffff || topk_before(acc[r][j], expert_of(j), bv, bi))) {
+          bv = acc[r][j];
+          bi = expert_of(j);
+        }
+      for (int off = LE / 2; off > 0; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off, LE);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off, LE);
+        if (oi != 0x7fffffff && (bi == 0x7fffffff || topk_before(ov, oi, bv, bi))) {
+          bv = ov;
+          bi = oi;
+        }
+      }
+      sel_v[s] = bv;
+      sel_i[s] = bi;
+      if (((bi % (4 * LE)) >> 2) == le) used |= 1u << ((bi / (4 * LE)) * 4 + (bi & 3));
+    }
+    if (le == 0 && t < T) {
+      float m = -INFINITY;
+      for (int j = 0; j < k; ++j) m = (sel_v[j] != sel_v[j] || sel_v[j] > m) ? sel_v[j] : m;
+      float ex[16], s = 0.0f;
+      for (int j = 0; j < k; ++j) {
+        ex[j] = expf(__fsub_rn(sel_v[j], m));
+        s = __fadd_rn(s, ex[j]);
+      }
+      for (int j = 0; j < k; ++j) {
+        idx_out[(int64_t)t * k + j] = sel_i[j];
+        w_out[(int64_t)t * k + j] = __fdiv_rn(ex[j], s);
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- dispatch
 constexpr int kDispThreads = 1024;  // entries per dispatch block (32 warps x 32)
 

@@ -10,14 +10,58 @@ inline size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 inline int64_t dispatch_blocks(int64_t n) { return (n + kDispThreads - 1) / kDispThreads; }
 
 // Router tile: lanes per token group LE, experts per lane EPL, tokens per
-// lane RT, warps per block, and the launch geometry that follows.
+// lane RT, warps per block, and the launch geometry that follows.  ring > 0
+// selects a k_router_ring instantiation (E % 8 == 0, E <= 64), 0 the
+// f32-staged k_router_topk.
 struct RouterPlan {
   int le, epl, rt, warps, dch;
   int64_t tpb, grid;
   size_t smem;
+  int ring;
+  char name[64];
 };
 
+// k_router_ring instantiations (LE, EPL, RT, WARPS, C, S), chosen from a
+// B200 sweep of the ring kernel (every variant bit-identical):
+//   1: E <= 8            <2,4,1,4,128,3>  (8192, 4096, 8) 49 us; (512, 4096, 8) 47 us
+//   2: E <= 16           <4,4,1,4,64,4>
+//   3: E <= 32           <8,4,2,4,64,4>
+//   4: E <= 64, T < 4096 <16,4,2,4,64,4>  (1000, 2056, 64) 50 us (16 tokens per block)
+//   5: E <= 64, T < 16K  <16,4,4,4,64,4>  (8192, 2048, 64) 105 us
+//   6: E <= 64, larger   <8,8,4,4,64,4>   (65536, 2048, 64) 471 us
+using RingA = RouterRing<2, 4, 1, 4, 128, 3>;
+using RingB = RouterRing<4, 4, 1, 4, 64, 4>;
+using RingC = RouterRing<8, 4, 2, 4, 64, 4>;
+using RingD = RouterRing<16, 4, 2, 4, 64, 4>;
+using RingE = RouterRing<16, 4, 4, 4, 64, 4>;
+using RingF = RouterRing<8, 8, 4, 4, 64, 4>;
+
+template <class R>
+void ring_plan(RouterPlan& p, int64_t T, int id, int le, int epl, int rt, int warps, int c,
+               int st) {
+  p.ring = id;
+  p.le = le;
+  p.epl = epl;
+  p.rt = rt;
+  p.warps = warps;
+  p.dch = c;
+  p.tpb = R::TPB;
+  p.smem = R::smem_bytes();
+  p.grid = (T + p.tpb - 1) / p.tpb;
+  snprintf(p.name, sizeof(p.name), "k_router_ring<%d,%d,%d,%d,%d,%d>", le, epl, rt, warps, c, st);
+}
+
 RouterPlan router_plan(int64_t T, int E) {
+  RouterPlan p;
+  if (E % 8 == 0 && E <= 64) {
+    if (E <= 8) ring_plan<RingA>(p, T, 1, 2, 4, 1, 4, 128, 3);
+    else if (E <= 16) ring_plan<RingB>(p, T, 2, 4, 4, 1, 4, 64, 4);
+    else if (E <= 32) ring_plan<RingC>(p, T, 3, 8, 4, 2, 4, 64, 4);
+    else if (T < 4096) ring_plan<RingD>(p, T, 4, 16, 4, 2, 4, 64, 4);
+    else if (T < 16384) ring_plan<RingE>(p, T, 5, 16, 4, 4, 4, 64, 4);
+    else ring_plan<RingF>(p, T, 6, 8, 8, 4, 4, 64, 4);
+    return p;
+  }
   // Lanes per token group LE (a power of two) and experts per lane EPL with
   // LE * EPL >= E; tokens per lane RT as large as still leaves at least 3/4
   // of the SMs a block (RT <= LE, RT * EPL <= 32 accumulators).  The shared
@@ -64,7 +108,7 @@ RouterPlan router_plan(int64_t T, int E) {
         break;
       }
   }
-  RouterPlan p;
+  p.ring = 0;
   p.le = le;
   p.epl = epl;
   p.rt = rt;
@@ -73,6 +117,7 @@ RouterPlan router_plan(int64_t T, int E) {
   p.tpb = tokens_per_block(rt);
   p.smem = (size_t)(p.tpb + le * epl) * (p.dch + 4) * 4;
   p.grid = (T + p.tpb - 1) / p.tpb;
+  snprintf(p.name, sizeof(p.name), "k_router_topk<%d,%d,%d,%d>", rt, epl, warps, dch);
   return p;
 }
 
@@ -99,7 +144,27 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
                                                        (int)D, E, k, le, idx, w);
     return REMORA_B200_OK;
   };
+  auto launch_ring = [&](auto kern) -> int {
+    RB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<(unsigned)grid, warps * 32, smem, st>>>(static_cast<const uint16_t*>(x),
+                                                       static_cast<const uint16_t*>(wr), (int)T,
+                                                       (int)D, E, k, idx, w);
+    return REMORA_B200_OK;
+  };
   int rc;
+  if (pl.ring) {
+    switch (pl.ring) {
+      case 1: rc = launch_ring(k_router_ring<2, 4, 1, 4, 128, 3>); break;
+      case 2: rc = launch_ring(k_router_ring<4, 4, 1, 4, 64, 4>); break;
+      case 3: rc = launch_ring(k_router_ring<8, 4, 2, 4, 64, 4>); break;
+      case 4: rc = launch_ring(k_router_ring<16, 4, 2, 4, 64, 4>); break;
+      case 5: rc = launch_ring(k_router_ring<16, 4, 4, 4, 64, 4>); break;
+      default: rc = launch_ring(k_router_ring<8, 8, 4, 4, 64, 4>); break;
+    }
+    if (rc) return rc;
+    RB_LAUNCH_CHECK();
+    return REMORA_B200_OK;
+  }
   switch (warps == 2 ? -1 : (pl.dch == 64 ? -2 : epl * 100 + rt)) {
     case -1: rc = launch(k_router_topk<2, 1, 2, 64>); break;
     case -2: rc = launch(k_router_topk<4, 4, 8, 64>); break;
@@ -173,7 +238,8 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
                    cudaStream_t st, const int32_t* seg_expert = nullptr, int n_seg = -1,
                    const int32_t* seg_start = nullptr, const int32_t* seg_end = nullptr,
                    const int32_t* dst_row = nullptr, const int32_t* dst_rank = nullptr,
-                   const PeerPtrs* dst = nullptr) {
+                   const PeerPtrs* dst = nullptr, const int32_t* gather_rows = nullptr,
+                   int gather_k = 1, int64_t a_rows = -1) {
   const int cols = swiglu ? 128 : 256;
   const int S = n_seg < 0 ? E : n_seg;
   RB_CHECK_ARG(E >= 1 && E <= GMaxE, "grouped_gemm: E=%d unsupported (1..%d)", E, GMaxE);
@@ -184,6 +250,8 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   RB_CHECK_ARG(rows < (1ll << 31) && K < (1ll << 31) && N < (1ll << 31),
                "grouped_gemm: sizes exceed 2^31");
   if (rows == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(!gather_rows || (a_rows >= 1 && a_rows < (1ll << 31) && gather_k >= 1),
+               "grouped_gemm: bad row gather");
   RB_CHECK_ARG(a && b0 && (out || dst) && (offsets || (seg_start && seg_end)) &&
                    (!swiglu || b1),
                "grouped_gemm: null pointer");
@@ -193,9 +261,12 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   CUtensorMap tA, tB0, tB1;
   int rc;
   {
-    uint64_t d[2] = {(uint64_t)K, (uint64_t)rows};
+    // With a row gather, A is the [a_rows, K] token matrix, copied row by row
+    // by the producer warp (this map is then unused); otherwise the [rows, K]
+    // dispatched matrix, loaded by tiles.
+    uint64_t d[2] = {(uint64_t)K, (uint64_t)(gather_rows ? a_rows : rows)};
     uint64_t s[1] = {(uint64_t)K * 2};
-    uint32_t box[2] = {GBK, GBM};
+    uint32_t box[2] = {GBK, gather_rows ? 1u : (uint32_t)GBM};
     if ((rc = make_tmap(&tA, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, s, box,
                         CU_TENSOR_MAP_SWIZZLE_128B)))
       return rc;
@@ -223,6 +294,9 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   sh.seg_dst_rank = dst ? dst_rank : nullptr;
   sh.dst = dst ? *dst : PeerPtrs{};
   sh.out = static_cast<uint16_t*>(out);
+  sh.gather_rows = gather_rows;
+  sh.gather_k = gather_k;
+  sh.gather_a = gather_rows ? static_cast<const uint16_t*>(a) : nullptr;
   // upper bound of the tile count: sum over experts of ceil(n_e / 128)
   const int64_t max_tiles = (rows / GBM + S) * (int64_t)sh.tiles_n;
   int grid = num_sms();
@@ -267,7 +341,7 @@ int combine_launch(const void* y, const int32_t* inv, const float* w, int64_t T,
 struct LayerWs {
   int32_t *idx, *counts, *offsets, *perm, *inv, *block_counts;
   float* w;
-  uint16_t *xs, *h, *y;
+  uint16_t *xs, *h, *y;  // dispatched rows [T*k, D], SwiGLU [T*k, F], expert outputs [T*k, D]
   size_t bytes;
 };
 
@@ -342,6 +416,16 @@ extern "C" int remora_b200_grouped_gemm_swiglu_bf16(const void* xs, const void* 
                                                     int64_t D, int64_t F, int E, void* stream) {
   clear_error();
   return grouped_launch(true, xs, wg, wu, h, offsets, rows, D, F, E, as_stream(stream));
+}
+
+extern "C" int remora_b200_grouped_gemm_swiglu_gather_bf16(
+    const void* x, const int32_t* perm, int64_t T, int k, const void* wg, const void* wu, void* h,
+    const int32_t* offsets, int64_t rows, int64_t D, int64_t F, int E, void* stream) {
+  clear_error();
+  RB_CHECK_ARG(T >= 1 && k >= 1 && perm && rows <= T * k,
+               "grouped_gemm_swiglu_gather: need T >= 1, k >= 1, perm, rows <= T*k");
+  return grouped_launch(true, x, wg, wu, h, offsets, rows, D, F, E, as_stream(stream), nullptr,
+                        -1, nullptr, nullptr, nullptr, nullptr, nullptr, perm, k, T);
 }
 
 extern "C" int remora_b200_grouped_gemm_bf16(const void* a, const void* w, void* y,

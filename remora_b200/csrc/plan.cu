@@ -44,9 +44,8 @@ void moe_plan(Text& t, int64_t T, int64_t D, int64_t F, int E, int k) {
         (long long)T, (long long)D, (long long)D, E, E, (long long)D, (long long)F, E,
         (long long)F, (long long)D, (long long)T, (long long)D, k,
         remora_b200_moe_workspace_bytes(T, D, F, E, k));
-  t.add("  rb::moe::k_router_topk<%d,%d,%d,%d>  grid %lld x block %d, smem %zu B (LE %d lanes "
-        "per token group)\n",
-        rp.rt, rp.epl, rp.warps, rp.dch, (long long)rp.grid, rp.warps * 32, rp.smem, rp.le);
+  t.add("  rb::moe::%s  grid %lld x block %d, smem %zu B (LE %d lanes per token group)\n",
+        rp.name, (long long)rp.grid, rp.warps * 32, rp.smem, rp.le);
   t.add("  rb::moe::k_dispatch_count  grid %lld x block %d, smem %d B\n", (long long)nb,
         kDispThreads, E * 4);
   t.add("  rb::moe::k_dispatch_scan  grid 1 x block %d\n", kScanThreads);
@@ -77,8 +76,8 @@ void hetero_plan(Text& t) {
         "bf16[4096,F_e], wd[e] bf16[F_e,4096], F_e = 14336 14336 8192 8192 4096 4096 2048 2048, "
         "out bf16[512,4096]), top-1, workspace %zu B\n",
         remora_b200_moe_hetero_workspace_bytes(T, D, F, 8, 1));
-  t.add("  rb::moe::k_router_topk<%d,%d,%d,%d>  grid %lld x block %d, smem %zu B\n", rp.rt,
-        rp.epl, rp.warps, rp.dch, (long long)rp.grid, rp.warps * 32, rp.smem);
+  t.add("  rb::moe::%s  grid %lld x block %d, smem %zu B\n", rp.name, (long long)rp.grid,
+        rp.warps * 32, rp.smem);
   t.add("  rb::moe::k_dispatch_count / k_dispatch_scan / k_dispatch_scatter  grid 1 / 1 / 1\n");
   t.add("  rb::moe::k_gather_rows  grid 64 x block 256 (512 rows of 4096 bf16)\n");
   t.add("  rb::moe::k_grouped_var<true>  grid %d x block %d, smem %u B (per-expert tensor maps; "
