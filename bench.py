@@ -571,7 +571,7 @@ def bench_moe_ep(args, world, rank, local):
         detail = {"kernel_ms": {"grouped_swiglu": t_up, "grouped_down": t_down,
                                 "router_topk": t_router},
                   "expert_tflops_layer": 6.0 * D * F * rows / (ms * 1e-3) / 1e12}
-        launches = 8  # router, dispatch count/scan/scatter, gather, SwiGLU, down, combine
+        launches = 8  # router, dispatch count/scan/scatter, row copy, SwiGLU, down, combine
     else:
         pep.profile = True
         phases = []

@@ -213,6 +213,14 @@ int remora_b200_moe_dispatch_noalloc(const int32_t* idx, int64_t T, int k, int E
 int remora_b200_moe_gather(const void* x, const int32_t* perm, int64_t rows, int k, int64_t D,
                            void* xs, void* stream);
 
+/* The same rows written token by token: xs[inv[t*k + j], :] = x[t, :] for
+ * t < T, j < k (inv from remora_b200_moe_dispatch).  Each token row is read
+ * once, so it moves (1 + k) * D * 2 bytes per token instead of 2 * k * D * 2;
+ * the fused layer uses this form for the one-hot dispatch of
+ * mixtral_moe_layer.mlir:28-31. */
+int remora_b200_moe_scatter(const void* x, const int32_t* inv, int64_t T, int k, int64_t D,
+                            void* xs, void* stream);
+
 /* Grouped expert GEMM with the SwiGLU epilogue (mixtral_moe_layer.mlir:32-41;
  * the outlined @expert_slot_N body, compiler/passes/ExpertOutlining.cpp:177-279):
  * for rows r of expert e (offsets[e] <= r < offsets[e+1]),
@@ -222,18 +230,6 @@ int remora_b200_moe_gather(const void* x, const int32_t* perm, int64_t rows, int
 int remora_b200_grouped_gemm_swiglu_bf16(const void* xs, const void* wg, const void* wu, void* h,
                                          const int32_t* offsets, int64_t rows, int64_t D,
                                          int64_t F, int E, void* stream);
-
-/* The SwiGLU grouped GEMM reading its rows straight from the tokens: row r
- * of the problem is x[perm[r] / k] (perm from remora_b200_moe_dispatch), so
- * the dispatched copy xs of the dispatch (mixtral_moe_layer.mlir:28-31) is
- * never written; the GEMM's producer warp copies each A tile's rows from x
- * into the swizzled shared-memory stage with cp.async.  x bf16
- * [T, D]; perm int32 [rows = T*k]; otherwise as above.  h is identical to
- * remora_b200_grouped_gemm_swiglu_bf16 on the gathered rows. */
-int remora_b200_grouped_gemm_swiglu_gather_bf16(const void* x, const int32_t* perm, int64_t T,
-                                                int k, const void* wg, const void* wu, void* h,
-                                                const int32_t* offsets, int64_t rows, int64_t D,
-                                                int64_t F, int E, void* stream);
 
 /* Grouped expert GEMM (the down projection, mixtral_moe_layer.mlir:42):
  * y[r, :] = a[r] . w[e] for the rows of expert e.  a bf16 [rows, K],

@@ -75,9 +75,8 @@ _SIGNATURES = {
     "remora_b200_moe_dispatch": ([P, I64, I, I, P, P, P, P, P, ctypes.c_size_t, P], I),
     "remora_b200_moe_dispatch_noalloc": ([P, I64, I, I, P, P, P, P, P], I),
     "remora_b200_moe_gather": ([P, P, I64, I, I64, P, P], I),
+    "remora_b200_moe_scatter": ([P, P, I64, I, I64, P, P], I),
     "remora_b200_grouped_gemm_swiglu_bf16": ([P, P, P, P, P, I64, I64, I64, I, P], I),
-    "remora_b200_grouped_gemm_swiglu_gather_bf16": ([P, P, I64, I, P, P, P, P, I64, I64, I64, I,
-                                                     P], I),
     "remora_b200_grouped_gemm_bf16": ([P, P, P, P, I64, I64, I64, I, P], I),
     "remora_b200_grouped_gemm_swiglu_segments_bf16": ([P, P, P, P, P, P, I, I64, I64, I64, I, P],
                                                       I),
@@ -319,6 +318,17 @@ def moe_dispatch(idx: torch.Tensor, E: int):
     return counts, offsets, perm, inv
 
 
+def moe_scatter(x: torch.Tensor, inv: torch.Tensor, k: int) -> torch.Tensor:
+    """xs[inv[t, j]] = x[t]: the dispatched rows, written token by token."""
+    _dev(x, inv)
+    _i32(inv)
+    T, D = x.shape
+    xs = torch.empty((T * k, D), dtype=x.dtype, device=x.device)
+    _check(lib().remora_b200_moe_scatter(x.contiguous().data_ptr(), inv.data_ptr(), T, k, D,
+                                         xs.data_ptr(), _stream(x)))
+    return xs
+
+
 def moe_gather(x: torch.Tensor, perm: torch.Tensor, k: int) -> torch.Tensor:
     _dev(x, perm)
     _i32(perm)
@@ -342,24 +352,6 @@ def grouped_gemm_swiglu(xs: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor,
     _check(lib().remora_b200_grouped_gemm_swiglu_bf16(
         xs.contiguous().data_ptr(), wg.contiguous().data_ptr(), wu.contiguous().data_ptr(),
         h.data_ptr(), offsets.data_ptr(), rows, D, F, E, _stream(xs)))
-    return h
-
-
-def grouped_gemm_swiglu_gather(x: torch.Tensor, perm: torch.Tensor, k: int, wg: torch.Tensor,
-                               wu: torch.Tensor, offsets: torch.Tensor,
-                               out: torch.Tensor | None = None) -> torch.Tensor:
-    """h = silu(x[perm // k] . wg[e]) * (x[perm // k] . wu[e]) over each expert's
-    row segment, the rows read from x by the GEMM itself (no gathered copy)."""
-    _dev(x, perm, wg, wu, offsets)
-    _bf16(x, wg, wu)
-    _i32(perm, offsets)
-    T, D = x.shape
-    rows = perm.numel()
-    E, _, F = wg.shape
-    h = torch.empty((rows, F), dtype=torch.bfloat16, device=x.device) if out is None else out
-    _check(lib().remora_b200_grouped_gemm_swiglu_gather_bf16(
-        x.contiguous().data_ptr(), perm.data_ptr(), T, k, wg.contiguous().data_ptr(),
-        wu.contiguous().data_ptr(), h.data_ptr(), offsets.data_ptr(), rows, D, F, E, _stream(x)))
     return h
 
 

@@ -615,6 +615,37 @@ __global__ void k_gather_rows(const uint16_t* __restrict__ x, const int32_t* __r
   }
 }
 
+// xs[inv[t*k + j], :] = x[t, :] for j < k: the same copy as k_gather_rows,
+// driven by tokens instead of destination rows, so each token row is read
+// from HBM once and written k times ((1 + k) * D * 2 bytes per token against
+// 2 * k * D * 2 for the gather).  One warp per token, up to 8 16-byte pieces
+// per lane loaded before the k stores of each.
+__global__ void k_scatter_rows(const uint16_t* __restrict__ x, const int32_t* __restrict__ inv,
+                               int64_t T, int k, int D, uint16_t* __restrict__ xs) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wpb = blockDim.x >> 5;
+  const int D8 = D / 8;
+  for (int64_t t = blockIdx.x * wpb + (threadIdx.x >> 5); t < T; t += (int64_t)gridDim.x * wpb) {
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * D);
+    for (int c0 = 0; c0 < D8; c0 += 8 * 32) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < D8) v[u] = __ldg(src + c);
+      }
+      for (int j = 0; j < k; ++j) {
+        uint4* dst = reinterpret_cast<uint4*>(xs + (int64_t)inv[t * k + j] * D);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int c = c0 + u * 32 + lane;
+          if (c < D8) dst[c] = v[u];
+        }
+      }
+    }
+  }
+}
+
 // ----------------------------------------------------------------- combine
 // out[t, :] = bf16( (((0 + w0*y0) + w1*y1) + ...) ) in slot order, each
 // product and sum rounded separately as the reference ops are.  One warp

@@ -50,13 +50,6 @@ struct GroupShape {
   const int32_t* seg_dst_row;
   const int32_t* seg_dst_rank;
   PeerPtrs dst;
-  // Optional row gather of the A operand: when set, row g of the grouped
-  // problem is row gather_rows[g] / gather_k of the A tensor map (the token
-  // of dispatch slot g), copied into the A stages by the producer warp, so
-  // the dispatched activations are never materialised.
-  const int32_t* gather_rows;
-  int gather_k;
-  const uint16_t* gather_a;   // [*, K] token matrix the rows are gathered from
 };
 
 // The expert-parallel dispatch carried by extra warps of the SwiGLU kernel:
@@ -264,7 +257,6 @@ __global__ void __launch_bounds__(GThreads, 1)
   int* s_exp = s_en + (GMaxE + 1);
   int* s_drow = s_exp + (GMaxE + 1);
   int* s_drank = s_drow + (GMaxE + 1);
-  int* s_tok = s_drank + (GMaxE + 1);  // [GBM] tokens of a gathered tile's rows
   // per epilogue warp: one [32 rows][128 B] staging tile, 1024-byte aligned
   uint8_t* epi_stage_base = smem + GEpiOffset;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -289,11 +281,8 @@ __global__ void __launch_bounds__(GThreads, 1)
       mt += max(s_en[q] - s_st[q], 0) / GBM + ((max(s_en[q] - s_st[q], 0) % GBM) ? 1 : 0);
     }
     s_mt[s.S] = mt;
-    // A gathering producer arrives on full[] from all 32 lanes (its A
-    // copies) besides lane 0's expect-tx arrival for B.
-    const uint32_t full_count = s.gather_rows ? 33u : 1u;
     for (int i = 0; i < GStages; ++i) {
-      mbar_init(&sm->full[i], full_count);
+      mbar_init(&sm->full[i], 1);
       mbar_init(&sm->empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -317,85 +306,7 @@ __global__ void __launch_bounds__(GThreads, 1)
   const int total_tiles = total_mt * s.tiles_n;
   constexpr int kColsPerTile = kSwiGLU ? 128 : 256;
 
-  if (warp == 0 && s.gather_rows) {
-    // Gathering producer: the whole warp.  Per tile it reads the 128 rows'
-    // tokens into shared memory; per k-block lane 0 waits for the stage,
-    // posts B's byte count and issues B's TMA loads, and the 32 lanes copy
-    // the A tile with cp.async (a warp instruction moves 4 rows x 128 bytes,
-    // 8 lanes per row) straight into the 128-byte-swizzled layout a TMA tile
-    // load would produce.  Each lane's copies arrive on the stage's full
-    // barrier when they land (cp.async.mbarrier.arrive.noinc: the producer
-    // never waits for them, so it runs up to GStages ahead as with TMA); the
-    // MMA thread fences the async proxy after its wait, so the tensor core
-    // reads what the generic-proxy copies wrote.  Rows past the segment's
-    // end repeat its last row (computed, never stored); columns past K are
-    // zero-filled.
-    if (lane == 0) {
-      tma_prefetch_desc(&tmB0);
-      if (kSwiGLU) tma_prefetch_desc(&tmB1);
-    }
-    const uint16_t* xa = s.gather_a;
-    const int K = s.K;
-    int stage = 0, issued = 0;
-    uint32_t phase = 0;
-    bool stop = false;
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      if (__shfl_sync(0xffffffffu, *abort_flag, 0)) break;
-      const TileInfo ti = group_tile(s, s_mt, s_st, s_en, s_exp, total_mt, t);
-      const int n0 = ti.n * kColsPerTile;
-      __syncwarp();  // the previous tile's token reads are done
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int g = min(ti.r0 + 32 * j + lane, ti.r_end - 1);
-        s_tok[32 * j + lane] = s.gather_rows[g] / s.gather_k;
-      }
-      __syncwarp();
-      for (int kb = 0; kb < s.num_kb; ++kb) {
-        bool ok = true;
-        if (lane == 0) {
-          ok = mbar_wait(&sm->empty[stage], phase ^ 1);
-          if (!ok) *abort_flag = 1;
-        }
-        if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) { stop = true; break; }
-        uint8_t* sa = smem + stage * GStageBytes;
-        uint8_t* sb = sa + GABytes;
-        if (lane == 0) {
-          mbar_arrive_expect_tx(&sm->full[stage], GBBytes);
-          if (kSwiGLU) {
-            for (int c = 0; c < 2; ++c) {
-              tma_load_3d(sb + c * 8192, &tmB0, &sm->full[stage], n0 + c * 64, kb * GBK, ti.e);
-              tma_load_3d(sb + 16384 + c * 8192, &tmB1, &sm->full[stage], n0 + c * 64, kb * GBK,
-                          ti.e);
-            }
-          } else {
-            for (int c = 0; c < 4; ++c)
-              tma_load_3d(sb + c * 8192, &tmB0, &sm->full[stage], n0 + c * 64, kb * GBK, ti.e);
-          }
-        }
-        const int ch = lane & 7;                 // 16-byte chunk of the row
-        const int col = kb * GBK + ch * 8;
-        const bool in_k = col < K;               // K % 8 == 0: chunks are in or out
-#pragma unroll 8
-        for (int j = 0; j < 32; ++j) {
-          const int r = 4 * j + (lane >> 3);
-          const uint16_t* src = xa + (int64_t)s_tok[r] * K + (in_k ? col : 0);
-          cp_async16(sa + r * 128 + ((ch ^ (r & 7)) << 4), src, in_k);
-        }
-        cp_async_arrive_noinc(&sm->full[stage]);
-        ++issued;
-        if (++stage == GStages) { stage = 0; phase ^= 1; }
-      }
-      if (stop) break;
-    }
-    cp_async_wait_all();
-    if (lane == 0 && *abort_flag) {
-      int st = stage, ph = phase;
-      for (int i = 0; i < GStages && i < issued; ++i) {
-        if (--st < 0) { st = GStages - 1; ph ^= 1; }
-        mbar_wait(&sm->full[st], ph);
-      }
-    }
-  } else if (warp == 0) {
+  if (warp == 0) {
     if (elect_one()) {
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB0);
@@ -434,7 +345,6 @@ __global__ void __launch_bounds__(GThreads, 1)
       }
     }
   } else if (warp == 1) {
-    const bool gather = s.gather_rows != nullptr;
     if (elect_one()) {
       constexpr uint32_t idesc = kSwiGLU ? idesc_bf16_f32(GBM, 128, 0, 1)
                                          : idesc_bf16_f32(GBM, 256, 0, 1);
@@ -448,7 +358,6 @@ __global__ void __launch_bounds__(GThreads, 1)
         for (int kb = 0; kb < s.num_kb; ++kb) {
           if (!mbar_wait(&sm->full[stage], phase)) { *abort_flag = 1; break; }
           tc_fence_after();
-          if (gather) fence_proxy_async_smem();  // A written by cp.async (generic proxy)
           const uint32_t sa = smem_u32(smem + stage * GStageBytes);
           const uint32_t sb = sa + GABytes;
 #pragma unroll

@@ -231,6 +231,20 @@ int gather_launch(const void* x, const int32_t* perm, int64_t rows, int k, int64
   return REMORA_B200_OK;
 }
 
+int scatter_launch(const void* x, const int32_t* inv, int64_t T, int k, int64_t D, void* xs,
+                   cudaStream_t st) {
+  RB_CHECK_ARG(T >= 0 && k >= 1 && D > 0 && D % 8 == 0, "scatter: bad sizes");
+  if (T == 0) return REMORA_B200_OK;
+  RB_CHECK_ARG(x && inv && xs && aligned16(x) && aligned16(xs),
+               "scatter: null or unaligned pointer");
+  const int64_t want = (T + 7) / 8;
+  const int64_t cap = (int64_t)num_sms() * 16;
+  k_scatter_rows<<<(unsigned)(want < cap ? want : cap), 256, 0, st>>>(
+      static_cast<const uint16_t*>(x), inv, T, k, (int)D, static_cast<uint16_t*>(xs));
+  RB_LAUNCH_CHECK();
+  return REMORA_B200_OK;
+}
+
 // Grouped GEMM over expert row segments.  a [rows, K]; b0 (and b1 for the
 // SwiGLU form) [E, K, N]; out [rows, N].  offsets [E+1] on the device.
 int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, void* out,
@@ -238,8 +252,7 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
                    cudaStream_t st, const int32_t* seg_expert = nullptr, int n_seg = -1,
                    const int32_t* seg_start = nullptr, const int32_t* seg_end = nullptr,
                    const int32_t* dst_row = nullptr, const int32_t* dst_rank = nullptr,
-                   const PeerPtrs* dst = nullptr, const int32_t* gather_rows = nullptr,
-                   int gather_k = 1, int64_t a_rows = -1) {
+                   const PeerPtrs* dst = nullptr) {
   const int cols = swiglu ? 128 : 256;
   const int S = n_seg < 0 ? E : n_seg;
   RB_CHECK_ARG(E >= 1 && E <= GMaxE, "grouped_gemm: E=%d unsupported (1..%d)", E, GMaxE);
@@ -250,8 +263,6 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   RB_CHECK_ARG(rows < (1ll << 31) && K < (1ll << 31) && N < (1ll << 31),
                "grouped_gemm: sizes exceed 2^31");
   if (rows == 0) return REMORA_B200_OK;
-  RB_CHECK_ARG(!gather_rows || (a_rows >= 1 && a_rows < (1ll << 31) && gather_k >= 1),
-               "grouped_gemm: bad row gather");
   RB_CHECK_ARG(a && b0 && (out || dst) && (offsets || (seg_start && seg_end)) &&
                    (!swiglu || b1),
                "grouped_gemm: null pointer");
@@ -261,12 +272,9 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   CUtensorMap tA, tB0, tB1;
   int rc;
   {
-    // With a row gather, A is the [a_rows, K] token matrix, copied row by row
-    // by the producer warp (this map is then unused); otherwise the [rows, K]
-    // dispatched matrix, loaded by tiles.
-    uint64_t d[2] = {(uint64_t)K, (uint64_t)(gather_rows ? a_rows : rows)};
+    uint64_t d[2] = {(uint64_t)K, (uint64_t)rows};
     uint64_t s[1] = {(uint64_t)K * 2};
-    uint32_t box[2] = {GBK, gather_rows ? 1u : (uint32_t)GBM};
+    uint32_t box[2] = {GBK, GBM};
     if ((rc = make_tmap(&tA, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d, s, box,
                         CU_TENSOR_MAP_SWIZZLE_128B)))
       return rc;
@@ -294,9 +302,6 @@ int grouped_launch(bool swiglu, const void* a, const void* b0, const void* b1, v
   sh.seg_dst_rank = dst ? dst_rank : nullptr;
   sh.dst = dst ? *dst : PeerPtrs{};
   sh.out = static_cast<uint16_t*>(out);
-  sh.gather_rows = gather_rows;
-  sh.gather_k = gather_k;
-  sh.gather_a = gather_rows ? static_cast<const uint16_t*>(a) : nullptr;
   // upper bound of the tile count: sum over experts of ceil(n_e / 128)
   const int64_t max_tiles = (rows / GBM + S) * (int64_t)sh.tiles_n;
   int grid = num_sms();
@@ -410,22 +415,18 @@ extern "C" int remora_b200_moe_gather(const void* x, const int32_t* perm, int64_
   return gather_launch(x, perm, rows, k, D, xs, as_stream(stream));
 }
 
+extern "C" int remora_b200_moe_scatter(const void* x, const int32_t* inv, int64_t T, int k,
+                                       int64_t D, void* xs, void* stream) {
+  clear_error();
+  return scatter_launch(x, inv, T, k, D, xs, as_stream(stream));
+}
+
 extern "C" int remora_b200_grouped_gemm_swiglu_bf16(const void* xs, const void* wg,
                                                     const void* wu, void* h,
                                                     const int32_t* offsets, int64_t rows,
                                                     int64_t D, int64_t F, int E, void* stream) {
   clear_error();
   return grouped_launch(true, xs, wg, wu, h, offsets, rows, D, F, E, as_stream(stream));
-}
-
-extern "C" int remora_b200_grouped_gemm_swiglu_gather_bf16(
-    const void* x, const int32_t* perm, int64_t T, int k, const void* wg, const void* wu, void* h,
-    const int32_t* offsets, int64_t rows, int64_t D, int64_t F, int E, void* stream) {
-  clear_error();
-  RB_CHECK_ARG(T >= 1 && k >= 1 && perm && rows <= T * k,
-               "grouped_gemm_swiglu_gather: need T >= 1, k >= 1, perm, rows <= T*k");
-  return grouped_launch(true, x, wg, wu, h, offsets, rows, D, F, E, as_stream(stream), nullptr,
-                        -1, nullptr, nullptr, nullptr, nullptr, nullptr, perm, k, T);
 }
 
 extern "C" int remora_b200_grouped_gemm_bf16(const void* a, const void* w, void* y,
@@ -488,7 +489,7 @@ extern "C" int remora_b200_moe_layer_bf16(const void* x, const void* wr, const v
   if ((rc = dispatch_launch(L.idx, T, k, E, L.counts, L.offsets, L.perm, L.inv, L.block_counts,
                             st)))
     return rc;
-  if ((rc = gather_launch(x, L.perm, n, k, D, L.xs, st))) return rc;
+  if ((rc = scatter_launch(x, L.inv, T, k, D, L.xs, st))) return rc;
   if ((rc = grouped_launch(true, L.xs, wg, wu, L.h, L.offsets, n, D, F, E, st))) return rc;
   if ((rc = grouped_launch(false, L.h, wd, nullptr, L.y, L.offsets, n, F, D, E, st))) return rc;
   return combine_launch(L.y, L.inv, L.w, T, k, D, out, st);

@@ -51,9 +51,10 @@ void moe_plan(Text& t, int64_t T, int64_t D, int64_t F, int E, int k) {
   t.add("  rb::moe::k_dispatch_scan  grid 1 x block %d\n", kScanThreads);
   t.add("  rb::moe::k_dispatch_scatter  grid %lld x block %d, smem %d B\n", (long long)nb,
         kDispThreads, 32 * E * 4);
-  const int64_t gather_grid = std::min<int64_t>((n + 7) / 8, (int64_t)num_sms() * 16);
-  t.add("  rb::moe::k_gather_rows  grid %lld x block 256 (%lld rows of %lld bf16)\n",
-        (long long)gather_grid, (long long)n, (long long)D);
+  const int64_t scatter_grid = std::min<int64_t>((T + 7) / 8, (int64_t)num_sms() * 16);
+  t.add("  rb::moe::k_scatter_rows  grid %lld x block 256 (%lld token rows of %lld bf16, %d "
+        "copies each)\n",
+        (long long)scatter_grid, (long long)T, (long long)D, k);
   const int64_t up_tiles = (n / GBM + E) * ((F + 127) / 128);
   const int64_t dn_tiles = (n / GBM + E) * ((D + 255) / 256);
   t.add("  rb::moe::k_grouped_gemm<true>  grid %lld x block %d, smem %u B (SwiGLU: gate|up "

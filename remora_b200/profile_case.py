@@ -2,8 +2,7 @@
 
     python -m remora_b200.profile_case <case> [--reps N] [--warmup W] [shape options]
 
-Cases: router, dispatch, gather, combine, swiglu, swiglu_gather, down, attention, gemm,
-layer, hetero.
+Cases: router, dispatch, gather, scatter, combine, swiglu, down, attention, gemm, layer, hetero.
 Each run fills its inputs with the seeded generator, launches the kernel
 `warmup` times, then `reps` times between CUDA events on the current
 stream, and prints one line: case, shape, time per launch, and the
@@ -54,6 +53,17 @@ def build_case(a):
                                                xs.data_ptr(),
                                                torch.cuda.current_stream().cuda_stream))
         return run, f"gather rows={T * k} D={D}", 2.0 * T * k * D * 2, "B"
+    if a.case == "scatter":
+        x, _, idx, _ = _routing(T, D, E, k)
+        _, _, _, inv = rb.moe_dispatch(idx, E)
+        xs = torch.empty(T * k, D, dtype=torch.bfloat16, device="cuda")
+        L = rb.lib()
+
+        def run():
+            rb._check(L.remora_b200_moe_scatter(x.data_ptr(), inv.data_ptr(), T, k, D,
+                                                xs.data_ptr(),
+                                                torch.cuda.current_stream().cuda_stream))
+        return run, f"scatter T={T} k={k} D={D}", (1.0 + k) * T * D * 2, "B"
     if a.case == "combine":
         _, _, idx, w = _routing(T, D, E, k)
         _, _, _, inv = rb.moe_dispatch(idx, E)
@@ -61,14 +71,6 @@ def build_case(a):
         out = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
         return (lambda: rb.moe_combine(y, inv, w, out=out), f"combine T={T} k={k} D={D}",
                 (k + 1.0) * T * D * 2, "B")
-    if a.case == "swiglu_gather":
-        x, _, idx, _ = _routing(T, D, E, k)
-        _, offsets, perm, _ = rb.moe_dispatch(idx, E)
-        wg, wu = _bf16((E, D, F), 32, 0.02), _bf16((E, D, F), 33, 0.02)
-        h = torch.empty(T * k, F, dtype=torch.bfloat16, device="cuda")
-        return (lambda: rb.grouped_gemm_swiglu_gather(x, perm, k, wg, wu, offsets, out=h),
-                f"grouped SwiGLU, rows gathered from x: rows={T * k} D={D} F={F} E={E}",
-                4.0 * T * k * D * F, "FLOP")
     if a.case in ("swiglu", "down"):
         x, _, idx, _ = _routing(T, D, E, k)
         _, offsets, perm, _ = rb.moe_dispatch(idx, E)

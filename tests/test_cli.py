@@ -52,7 +52,7 @@ def test_usage_and_missing_file(cli, tmp_path):
     ("moe_simple", "remora_b200_moe_layer_bf16(x bf16[8,32]",
      ["k_router_topk", "k_dispatch_scan", "k_grouped_gemm<true>", "k_combine<2>"]),
     ("moe_mixtral", "remora_b200_moe_layer_bf16(x bf16[512,4096]",
-     ["k_router_ring<2,4,1,4,128,3>", "k_gather_rows", "k_grouped_gemm<false>"]),
+     ["k_router_ring<2,4,1,4,128,3>", "k_scatter_rows", "k_grouped_gemm<false>"]),
     ("moe_hetero", "remora_b200_moe_hetero_layer_bf16",
      ["k_grouped_var<true>", "k_grouped_var<false>", "F_e = 14336 14336 8192"])])
 def test_emit_ptx_prints_the_launch_plan_without_gpu(cli, tmp_path, sig, entry, kernels):
