@@ -469,6 +469,31 @@ def _e2e(step, ins, outs, args, world, dev):
     return ms, h2d, d2h
 
 
+def _e2e_moe_host(rb, x, wr, wg, wu, wd, k, args, dev):
+    """The one-GPU layer end to end through remora_b200_moe_layer_host_bf16:
+    tokens in pinned host memory go up and the output comes back in chunks
+    of 8192 tokens, overlapped with the layer's kernels.  Returns (ms, h2d,
+    d2h bytes per step)."""
+    import torch
+
+    T, D = x.shape
+    E, _, F = wg.shape
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((T, D), dtype=torch.bfloat16, pin_memory=True)
+    ws = torch.empty(rb.lib().remora_b200_moe_layer_host_workspace_bytes(T, D, F, E, k, 0),
+                     dtype=torch.uint8, device=dev)
+
+    def e2e_step():
+        rb.moe_layer_host(x_host, wr, wg, wu, wd, k, out_host=out_host, workspace=ws)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    ms = _cuda_time(e2e_step, max(3, min(args.steps, 10)), dev)
+    nbytes = T * D * 2
+    return ms, nbytes, nbytes
+
+
 def _line(args, world, value, unit, ms, scaling, dtype, data, roofline, e2e, launches, clocks,
           detail):
     return {"metric": METRIC, "value": value, "unit": unit, "n_gpus": world,
@@ -550,7 +575,10 @@ def bench_moe_ep(args, world, rank, local):
     ms_local, clocks = _timed(step, args, world, dev, local)
     rank_ms = all_ranks(ms_local, world)
     ms = max(rank_ms)
-    e2e_ms, h2d, d2h = _e2e(step, [x], [out], args, world, dev)
+    if world == 1:
+        e2e_ms, h2d, d2h = _e2e_moe_host(rb, x, wr, wg, wu, wd, k, args, dev)
+    else:
+        e2e_ms, h2d, d2h = _e2e(step, [x], [out], args, world, dev)
 
     # dominant kernel, timed by itself with CUDA events after the timed region
     if world == 1:
@@ -620,7 +648,10 @@ def bench_moe(args, world, rank, local):
 
     ms_local, clocks = _timed(step, args, world, dev, local)
     ms = max_over_ranks(ms_local, world)
-    e2e_ms, h2d, d2h = _e2e(step, [x], [out], args, world, dev)
+    e2e_ms, h2d, d2h = _e2e_moe_host(rb, x, wr, wg, wu, wd, k, args, dev)
+    barrier(world)
+    e2e_ms = max_over_ranks(e2e_ms, world)
+    h2d, d2h = h2d * world, d2h * world
     idx, w = rb.moe_router_topk(x, wr, k)
     counts, offsets, perm, inv = rb.moe_dispatch(idx, E)
     xs = rb.moe_gather(x, perm, k)

@@ -261,7 +261,7 @@ int remora_b200_moe_combine_bf16(const void* y, const int32_t* inv, const float*
 /* Bytes of device workspace remora_b200_moe_layer_bf16 needs. */
 size_t remora_b200_moe_workspace_bytes(int64_t T, int64_t D, int64_t F, int E, int k);
 
-/* The whole MoE layer: router -> dispatch -> gather -> SwiGLU grouped GEMM
+/* The whole MoE layer: router -> dispatch -> row copy -> SwiGLU grouped GEMM
  * -> down grouped GEMM -> combine, stream-ordered, no host synchronisation.
  * x bf16 [T, D]; wr bf16 [D, E]; wg, wu bf16 [E, D, F]; wd bf16 [E, F, D];
  * out bf16 [T, D].  F % 32 == 0, D % 32 == 0.  The workspace (caller
@@ -270,6 +270,25 @@ size_t remora_b200_moe_workspace_bytes(int64_t T, int64_t D, int64_t F, int E, i
 int remora_b200_moe_layer_bf16(const void* x, const void* wr, const void* wg, const void* wu,
                                const void* wd, void* out, int64_t T, int64_t D, int64_t F, int E,
                                int k, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same layer with the tokens and the output in HOST memory, for callers
+ * whose activations live on the host (remora's harness fills host vectors,
+ * compiler/gpu_tests.cpp:48-56): the tokens go up and the output comes back
+ * in chunks of chunk_tokens (0 = 8192) on two copy streams of the library's
+ * own, overlapped with the layer's kernels on `stream` (chunk c computes
+ * while chunk c+1 goes up and chunk c-1 comes down; tokens are independent,
+ * so the output is bit-identical to remora_b200_moe_layer_bf16).  Weights
+ * and router are device pointers.  x_host and out_host should be pinned
+ * (cudaHostAlloc / cudaHostRegister); pageable memory is correct but its
+ * copies do not overlap.  The call only enqueues work: out_host is complete
+ * once `stream` has reached this point (synchronise it before reading).
+ * The copy streams and events are created once per (thread, device). */
+size_t remora_b200_moe_layer_host_workspace_bytes(int64_t T, int64_t D, int64_t F, int E, int k,
+                                                  int64_t chunk_tokens);
+int remora_b200_moe_layer_host_bf16(const void* x_host, const void* wr, const void* wg,
+                                    const void* wu, const void* wd, void* out_host, int64_t T,
+                                    int64_t D, int64_t F, int E, int k, int64_t chunk_tokens,
+                                    void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------
  * Heterogeneous MoE: experts of different FFN widths

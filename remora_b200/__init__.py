@@ -85,6 +85,9 @@ _SIGNATURES = {
     "remora_b200_moe_workspace_bytes": ([I64, I64, I64, I, I], ctypes.c_size_t),
     "remora_b200_moe_layer_bf16": ([P, P, P, P, P, P, I64, I64, I64, I, I, P, ctypes.c_size_t, P],
                                    I),
+    "remora_b200_moe_layer_host_workspace_bytes": ([I64, I64, I64, I, I, I64], ctypes.c_size_t),
+    "remora_b200_moe_layer_host_bf16": ([P, P, P, P, P, P, I64, I64, I64, I, I, I64, P,
+                                         ctypes.c_size_t, P], I),
     "remora_b200_moe_ep_scatter_bf16": ([P, P, P, I64, I, I64, I, I, I, I64, P, P, P], I),
     "remora_b200_moe_ep_barrier": ([P, P, I, I, I, P], I),
     "remora_b200_moe_ep_segments": ([P, I, I, I64, P, P], I),
@@ -436,6 +439,32 @@ def moe_layer(x: torch.Tensor, wr: torch.Tensor, wg: torch.Tensor, wu: torch.Ten
         wu.contiguous().data_ptr(), wd.contiguous().data_ptr(), out.data_ptr(), T, D, F, E, k,
         workspace.data_ptr(), workspace.numel(), _stream(x)))
     return out
+
+
+def moe_layer_host(x_host: torch.Tensor, wr: torch.Tensor, wg: torch.Tensor, wu: torch.Tensor,
+                   wd: torch.Tensor, k: int, out_host: torch.Tensor | None = None,
+                   chunk_tokens: int = 0, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The MoE layer on tokens in (pinned) host memory: chunks go up, through
+    the layer and back on copy streams overlapped with the kernels.  Returns
+    out_host after enqueueing; synchronise the current stream before reading."""
+    if x_host.is_cuda or (out_host is not None and out_host.is_cuda):
+        raise ValueError("moe_layer_host takes host tensors for x and out")
+    _dev(wr, wg, wu, wd)
+    _bf16(x_host, wr, wg, wu, wd)
+    T, D = x_host.shape
+    E, _, F = wg.shape
+    need = lib().remora_b200_moe_layer_host_workspace_bytes(T, D, F, E, k, chunk_tokens)
+    if need == 0:
+        raise ValueError("moe_layer_host: unsupported sizes")
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=wg.device)
+    if out_host is None:
+        out_host = torch.empty((T, D), dtype=torch.bfloat16, pin_memory=True)
+    _check(lib().remora_b200_moe_layer_host_bf16(
+        x_host.contiguous().data_ptr(), wr.contiguous().data_ptr(), wg.contiguous().data_ptr(),
+        wu.contiguous().data_ptr(), wd.contiguous().data_ptr(), out_host.data_ptr(), T, D, F, E,
+        k, chunk_tokens, workspace.data_ptr(), workspace.numel(), _stream(wg)))
+    return out_host
 
 
 def _ptrs(ts):

@@ -1,5 +1,7 @@
 // moe_host.cu -- C ABI launchers of the MoE layer (router, dispatch, gather,
 // grouped expert GEMMs, combine) and the fused layer entry point.
+#include <algorithm>
+
 #include "runtime.cuh"
 
 namespace rb {
@@ -373,6 +375,72 @@ inline LayerWs layer_ws(void* base, int64_t T, int64_t D, int64_t F, int E, int 
   return L;
 }
 
+// The layer's launches on one stream over a carved workspace (sizes checked
+// by the callers).
+int layer_run(const void* x, const void* wr, const void* wg, const void* wu, const void* wd,
+              void* out, int64_t T, int64_t D, int64_t F, int E, int k, const LayerWs& L,
+              cudaStream_t st) {
+  const int64_t n = T * k;
+  int rc;
+  if ((rc = router_launch(x, wr, T, D, E, k, L.idx, L.w, st))) return rc;
+  if ((rc = dispatch_launch(L.idx, T, k, E, L.counts, L.offsets, L.perm, L.inv, L.block_counts,
+                            st)))
+    return rc;
+  if ((rc = scatter_launch(x, L.inv, T, k, D, L.xs, st))) return rc;
+  if ((rc = grouped_launch(true, L.xs, wg, wu, L.h, L.offsets, n, D, F, E, st))) return rc;
+  if ((rc = grouped_launch(false, L.h, wd, nullptr, L.y, L.offsets, n, F, D, E, st))) return rc;
+  return combine_launch(L.y, L.inv, L.w, T, k, D, out, st);
+}
+
+int layer_check(const void* x, const void* wr, const void* wg, const void* wu, const void* wd,
+                const void* out, int64_t T, int64_t D, int64_t F, int E, int k) {
+  RB_CHECK_ARG(T >= 0 && D > 0 && F > 0 && E >= 1 && E <= GMaxE && k >= 1 && k <= 16 && k <= E,
+               "moe_layer: bad sizes");
+  RB_CHECK_ARG(T <= INT32_MAX / k, "moe_layer: T*k exceeds the int32 range of the routing tables");
+  RB_CHECK_ARG(T == 0 || (x && wr && wg && wu && wd && out), "moe_layer: null pointer");
+  return REMORA_B200_OK;
+}
+
+// Copy streams and events of the host-buffer layer, one set per (thread,
+// device), created on first use and kept for the life of the thread.
+struct HostPipe {
+  cudaStream_t up = nullptr, down = nullptr;
+  cudaEvent_t start = nullptr, h2d[2] = {}, done[2] = {}, d2h[2] = {};
+};
+
+int host_pipe(HostPipe** out) {
+  static thread_local HostPipe pipes[16];
+  int dev = 0;
+  RB_CUDA(cudaGetDevice(&dev));
+  RB_CHECK_ARG(dev >= 0 && dev < 16, "moe_layer_host: device %d out of range", dev);
+  HostPipe& p = pipes[dev];
+  if (!p.up) {
+    RB_CUDA(cudaStreamCreateWithFlags(&p.up, cudaStreamNonBlocking));
+    RB_CUDA(cudaStreamCreateWithFlags(&p.down, cudaStreamNonBlocking));
+    RB_CUDA(cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming));
+    for (int i = 0; i < 2; ++i) {
+      RB_CUDA(cudaEventCreateWithFlags(&p.h2d[i], cudaEventDisableTiming));
+      RB_CUDA(cudaEventCreateWithFlags(&p.done[i], cudaEventDisableTiming));
+      RB_CUDA(cudaEventCreateWithFlags(&p.d2h[i], cudaEventDisableTiming));
+    }
+  }
+  *out = &p;
+  return REMORA_B200_OK;
+}
+
+constexpr int64_t kHostChunkTokens = 8192;
+
+int64_t host_chunk(int64_t T, int64_t chunk_tokens) {
+  const int64_t c = chunk_tokens > 0 ? chunk_tokens : kHostChunkTokens;
+  return T < c ? (T > 0 ? T : 1) : c;
+}
+
+// Workspace of the host-buffer layer: the layer workspace of one chunk, then
+// two token buffers and two output buffers of one chunk each.
+size_t host_ws_bytes(int64_t chunk, int64_t D, int64_t F, int E, int k) {
+  return layer_ws(nullptr, chunk, D, F, E, k).bytes + 4 * align256((size_t)chunk * D * 2);
+}
+
 }  // namespace moe
 }  // namespace rb
 
@@ -473,24 +541,74 @@ extern "C" int remora_b200_moe_layer_bf16(const void* x, const void* wr, const v
                                           int64_t D, int64_t F, int E, int k, void* workspace,
                                           size_t workspace_bytes, void* stream) {
   clear_error();
-  RB_CHECK_ARG(T >= 0 && D > 0 && F > 0 && E >= 1 && E <= GMaxE && k >= 1 && k <= 16 && k <= E,
-               "moe_layer: bad sizes");
-  RB_CHECK_ARG(T <= INT32_MAX / k, "moe_layer: T*k exceeds the int32 range of the routing tables");
+  int rc;
+  if ((rc = layer_check(x, wr, wg, wu, wd, out, T, D, F, E, k))) return rc;
   if (T == 0) return REMORA_B200_OK;
-  RB_CHECK_ARG(x && wr && wg && wu && wd && out && workspace, "moe_layer: null pointer");
+  RB_CHECK_ARG(workspace, "moe_layer: null workspace");
   LayerWs L = layer_ws(workspace, T, D, F, E, k);
   RB_CHECK_ARG(workspace_bytes >= L.bytes, "moe_layer: workspace of %zu bytes, %zu needed",
                workspace_bytes, L.bytes);
   RB_CHECK_ARG(aligned16(workspace), "moe_layer: workspace must be 16-byte aligned");
-  cudaStream_t st = as_stream(stream);
-  const int64_t n = T * k;
-  int rc;
-  if ((rc = router_launch(x, wr, T, D, E, k, L.idx, L.w, st))) return rc;
-  if ((rc = dispatch_launch(L.idx, T, k, E, L.counts, L.offsets, L.perm, L.inv, L.block_counts,
-                            st)))
-    return rc;
-  if ((rc = scatter_launch(x, L.inv, T, k, D, L.xs, st))) return rc;
-  if ((rc = grouped_launch(true, L.xs, wg, wu, L.h, L.offsets, n, D, F, E, st))) return rc;
-  if ((rc = grouped_launch(false, L.h, wd, nullptr, L.y, L.offsets, n, F, D, E, st))) return rc;
-  return combine_launch(L.y, L.inv, L.w, T, k, D, out, st);
+  return layer_run(x, wr, wg, wu, wd, out, T, D, F, E, k, L, as_stream(stream));
 }
+
+extern "C" size_t remora_b200_moe_layer_host_workspace_bytes(int64_t T, int64_t D, int64_t F,
+                                                             int E, int k, int64_t chunk_tokens) {
+  if (T < 0 || D <= 0 || F <= 0 || E < 1 || E > GMaxE || k < 1 || k > 16 || k > E ||
+      chunk_tokens < 0 || T > INT32_MAX / k)
+    return 0;
+  return host_ws_bytes(host_chunk(T, chunk_tokens), D, F, E, k);
+}
+
+extern "C" int remora_b200_moe_layer_host_bf16(const void* x_host, const void* wr, const void* wg,
+                                               const void* wu, const void* wd, void* out_host,
+                                               int64_t T, int64_t D, int64_t F, int E, int k,
+                                               int64_t chunk_tokens, void* workspace,
+                                               size_t workspace_bytes, void* stream) {
+  clear_error();
+  int rc;
+  if ((rc = layer_check(x_host, wr, wg, wu, wd, out_host, T, D, F, E, k))) return rc;
+  RB_CHECK_ARG(chunk_tokens >= 0, "moe_layer_host: chunk_tokens must be >= 0");
+  if (T == 0) return REMORA_B200_OK;
+  const int64_t C = host_chunk(T, chunk_tokens);
+  RB_CHECK_ARG(workspace && aligned16(workspace), "moe_layer_host: null or unaligned workspace");
+  RB_CHECK_ARG(workspace_bytes >= host_ws_bytes(C, D, F, E, k),
+               "moe_layer_host: workspace of %zu bytes, %zu needed", workspace_bytes,
+               host_ws_bytes(C, D, F, E, k));
+  LayerWs L = layer_ws(workspace, C, D, F, E, k);
+  uint8_t* bufs = static_cast<uint8_t*>(workspace) + L.bytes;
+  const size_t cb = align256((size_t)C * D * 2);
+  uint8_t* xb[2] = {bufs, bufs + cb};
+  uint8_t* ob[2] = {bufs + 2 * cb, bufs + 3 * cb};
+  HostPipe* p = nullptr;
+  if ((rc = host_pipe(&p))) return rc;
+  cudaStream_t st = as_stream(stream);
+  // Copies start after the caller's earlier work on `stream`; chunk c's
+  // tokens go up on one stream while chunk c-1 computes on `stream` and chunk
+  // c-2's output comes down on another; buffers are reused two chunks later.
+  RB_CUDA(cudaEventRecord(p->start, st));
+  RB_CUDA(cudaStreamWaitEvent(p->up, p->start, 0));
+  RB_CUDA(cudaStreamWaitEvent(p->down, p->start, 0));
+  const int64_t nc = (T + C - 1) / C;
+  for (int64_t c = 0; c < nc; ++c) {
+    const int b = (int)(c & 1);
+    const int64_t t0 = c * C, tc = std::min<int64_t>(C, T - t0);
+    const size_t bytes = (size_t)tc * D * 2;
+    if (c >= 2) RB_CUDA(cudaStreamWaitEvent(p->up, p->done[b], 0));
+    RB_CUDA(cudaMemcpyAsync(xb[b], static_cast<const uint8_t*>(x_host) + (size_t)t0 * D * 2,
+                            bytes, cudaMemcpyHostToDevice, p->up));
+    RB_CUDA(cudaEventRecord(p->h2d[b], p->up));
+    RB_CUDA(cudaStreamWaitEvent(st, p->h2d[b], 0));
+    if (c >= 2) RB_CUDA(cudaStreamWaitEvent(st, p->d2h[b], 0));
+    if ((rc = layer_run(xb[b], wr, wg, wu, wd, ob[b], tc, D, F, E, k, L, st))) return rc;
+    RB_CUDA(cudaEventRecord(p->done[b], st));
+    RB_CUDA(cudaStreamWaitEvent(p->down, p->done[b], 0));
+    RB_CUDA(cudaMemcpyAsync(static_cast<uint8_t*>(out_host) + (size_t)t0 * D * 2, ob[b], bytes,
+                            cudaMemcpyDeviceToHost, p->down));
+    RB_CUDA(cudaEventRecord(p->d2h[b], p->down));
+  }
+  // the call is complete on `stream` once the last output chunk is down
+  RB_CUDA(cudaStreamWaitEvent(st, p->d2h[(nc - 1) & 1], 0));
+  return REMORA_B200_OK;
+}
+

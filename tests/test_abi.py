@@ -124,3 +124,23 @@ def test_heterogeneous_and_nccl_entry_points_validate_without_gpu():
     assert L.remora_b200_peer_open(None, ctypes.byref(out)) == rb.ERR_INVALID
     assert L.remora_b200_peer_close(None) == rb.ERR_INVALID
     assert L.remora_b200_peer_free(None) == rb.OK
+
+
+def test_host_buffer_layer_validates_before_cuda():
+    import remora_b200 as rb
+
+    L = rb.lib()
+    assert L.remora_b200_moe_layer_host_workspace_bytes(65536, 2048, 1536, 64, 8, 0) > 0
+    # one chunk's workspace, whatever T is
+    assert (L.remora_b200_moe_layer_host_workspace_bytes(65536, 2048, 1536, 64, 8, 4096) ==
+            L.remora_b200_moe_layer_host_workspace_bytes(8192, 2048, 1536, 64, 8, 4096))
+    assert L.remora_b200_moe_layer_host_workspace_bytes(100, 256, 128, 8, 9, 0) == 0   # k > E
+    assert L.remora_b200_moe_layer_host_workspace_bytes(100, 256, 128, 8, 2, -1) == 0
+    p = ctypes.c_void_p(16)
+    rc = L.remora_b200_moe_layer_host_bf16(p, p, p, p, p, p, 100, 256, 128, 8, 2, -5, p, 1 << 30,
+                                           None)
+    assert rc == rb.ERR_INVALID and "chunk" in rb.last_error()
+    rc = L.remora_b200_moe_layer_host_bf16(p, p, p, p, p, p, 100, 256, 128, 8, 2, 0, None, 0, None)
+    assert rc == rb.ERR_INVALID and "workspace" in rb.last_error()
+    rc = L.remora_b200_moe_layer_host_bf16(p, p, p, p, p, p, 100, 256, 128, 8, 2, 0, p, 16, None)
+    assert rc == rb.ERR_INVALID and "workspace" in rb.last_error()

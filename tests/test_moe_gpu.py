@@ -154,6 +154,26 @@ def test_moe_layer_parity(rb, orc, T, D, F, E, k):
     assert norm_err(got, r) <= TOL
 
 
+@pytest.mark.parametrize("T,chunk", [(1000, 256), (777, 0), (4096, 1000)])
+def test_moe_layer_host_buffers_match_device_layer(rb, orc, T, chunk):
+    """Tokens and output in pinned host memory, copied in chunks (a ragged
+    last chunk; one chunk when chunk_tokens=0 covers T) overlapped with the
+    layer: bit-identical to the device-buffer layer."""
+    D, F, E, k = 256, 128, 16, 4
+    x, wr, wg, wu, wd = _moe_inputs(orc, T, D, F, E)
+    dev = [from_np_bf16(a) for a in (x, wr, wg, wu, wd)]
+    ref = rb.moe_layer(*dev, k=k)
+    x_host = dev[0].cpu().pin_memory()
+    out = rb.moe_layer_host(x_host, *dev[1:], k=k, chunk_tokens=chunk)
+    torch.cuda.current_stream().synchronize()
+    rb.synchronize_and_check()
+    assert torch.equal(out.view(torch.int16), ref.cpu().view(torch.int16))
+    # a second call reuses the library's copy streams and events
+    out2 = rb.moe_layer_host(x_host, *dev[1:], k=k, chunk_tokens=chunk)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(out2.view(torch.int16), ref.cpu().view(torch.int16))
+
+
 def test_moe_layer_deterministic(rb, orc):
     x, wr, wg, wu, wd = _moe_inputs(orc, 256, 256, 128, 8)
     args = [from_np_bf16(a) for a in (x, wr, wg, wu, wd)]
