@@ -402,10 +402,13 @@ int layer_check(const void* x, const void* wr, const void* wg, const void* wu, c
 }
 
 // Copy streams and events of the host-buffer layer, one set per (thread,
-// device), created on first use and kept for the life of the thread.
+// device), created on first use and kept for the life of the thread; made
+// again when the device's context has changed (after a cudaDeviceReset the
+// old handles belong to a destroyed context).
 struct HostPipe {
   cudaStream_t up = nullptr, down = nullptr;
   cudaEvent_t start = nullptr, h2d[2] = {}, done[2] = {}, d2h[2] = {};
+  unsigned long long ctx_id = 0;
 };
 
 int host_pipe(HostPipe** out) {
@@ -414,7 +417,10 @@ int host_pipe(HostPipe** out) {
   RB_CUDA(cudaGetDevice(&dev));
   RB_CHECK_ARG(dev >= 0 && dev < 16, "moe_layer_host: device %d out of range", dev);
   HostPipe& p = pipes[dev];
+  const unsigned long long ctx = current_ctx_id();
+  if (p.up && ctx != p.ctx_id) p = HostPipe{};
   if (!p.up) {
+    p.ctx_id = ctx;  // 0 before the context exists: the next call makes the set again
     RB_CUDA(cudaStreamCreateWithFlags(&p.up, cudaStreamNonBlocking));
     RB_CUDA(cudaStreamCreateWithFlags(&p.down, cudaStreamNonBlocking));
     RB_CUDA(cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming));

@@ -49,31 +49,6 @@ struct NoAllocSlot {
 static NoAllocSlot g_noalloc[kMaxDevices] = {};
 static std::mutex g_noalloc_mu;
 
-using CtxGetCurrentFn = CUresult (*)(CUcontext*);
-using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
-
-// Unique id of the current thread's CUDA context (ids are never reused
-// within a process, unlike context handles).  0 when the driver cannot say.
-static unsigned long long current_ctx_id() {
-  static CtxGetCurrentFn get_cur = nullptr;
-  static CtxGetIdFn get_id = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
-    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      get_id = reinterpret_cast<CtxGetIdFn>(p);
-  });
-  CUcontext c = nullptr;
-  unsigned long long id = 0;
-  if (get_cur && get_id && get_cur(&c) == CUDA_SUCCESS && c && get_id(c, &id) == CUDA_SUCCESS)
-    return id;
-  return 0;
-}
 
 // Device address of the scratch array on the current device, looked up once
 // per device and context.  If the context id cannot be read, the address is

@@ -105,6 +105,32 @@ inline int num_sms() {
   return n;
 }
 
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// Unique id of the current thread's CUDA context (ids are never reused
+// within a process, unlike context handles).  0 when the driver cannot say.
+inline unsigned long long current_ctx_id() {
+  static CtxGetCurrentFn get_cur = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<CtxGetCurrentFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (get_cur && get_id && get_cur(&c) == CUDA_SUCCESS && c && get_id(c, &id) == CUDA_SUCCESS)
+    return id;
+  return 0;
+}
+
 // Reads and clears the device error word (synchronises the stream).
 inline int collect_device_error(cudaStream_t st) {
   int v = 0, zero = 0;
