@@ -420,7 +420,6 @@ int host_pipe(HostPipe** out) {
   const unsigned long long ctx = current_ctx_id();
   if (p.up && ctx != p.ctx_id) p = HostPipe{};
   if (!p.up) {
-    p.ctx_id = ctx;  // 0 before the context exists: the next call makes the set again
     RB_CUDA(cudaStreamCreateWithFlags(&p.up, cudaStreamNonBlocking));
     RB_CUDA(cudaStreamCreateWithFlags(&p.down, cudaStreamNonBlocking));
     RB_CUDA(cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming));
@@ -429,6 +428,7 @@ int host_pipe(HostPipe** out) {
       RB_CUDA(cudaEventCreateWithFlags(&p.done[i], cudaEventDisableTiming));
       RB_CUDA(cudaEventCreateWithFlags(&p.d2h[i], cudaEventDisableTiming));
     }
+    p.ctx_id = current_ctx_id();  // the context exists now
   }
   *out = &p;
   return REMORA_B200_OK;
