@@ -419,16 +419,18 @@ int host_pipe(HostPipe** out) {
   HostPipe& p = pipes[dev];
   const unsigned long long ctx = current_ctx_id();
   if (p.up && ctx != p.ctx_id) p = HostPipe{};
-  if (!p.up) {
-    RB_CUDA(cudaStreamCreateWithFlags(&p.up, cudaStreamNonBlocking));
-    RB_CUDA(cudaStreamCreateWithFlags(&p.down, cudaStreamNonBlocking));
-    RB_CUDA(cudaEventCreateWithFlags(&p.start, cudaEventDisableTiming));
+  if (!p.up) {  // built whole before it is kept, so a failed call leaves no half set
+    HostPipe q;
+    RB_CUDA(cudaStreamCreateWithFlags(&q.up, cudaStreamNonBlocking));
+    RB_CUDA(cudaStreamCreateWithFlags(&q.down, cudaStreamNonBlocking));
+    RB_CUDA(cudaEventCreateWithFlags(&q.start, cudaEventDisableTiming));
     for (int i = 0; i < 2; ++i) {
-      RB_CUDA(cudaEventCreateWithFlags(&p.h2d[i], cudaEventDisableTiming));
-      RB_CUDA(cudaEventCreateWithFlags(&p.done[i], cudaEventDisableTiming));
-      RB_CUDA(cudaEventCreateWithFlags(&p.d2h[i], cudaEventDisableTiming));
+      RB_CUDA(cudaEventCreateWithFlags(&q.h2d[i], cudaEventDisableTiming));
+      RB_CUDA(cudaEventCreateWithFlags(&q.done[i], cudaEventDisableTiming));
+      RB_CUDA(cudaEventCreateWithFlags(&q.d2h[i], cudaEventDisableTiming));
     }
-    p.ctx_id = current_ctx_id();  // the context exists now
+    q.ctx_id = current_ctx_id();  // the context exists now
+    p = q;
   }
   *out = &p;
   return REMORA_B200_OK;
