@@ -472,8 +472,9 @@ def _e2e(step, ins, outs, args, world, dev):
 def _e2e_moe_host(rb, x, wr, wg, wu, wd, k, args, dev):
     """The one-GPU layer end to end through remora_b200_moe_layer_host_bf16:
     tokens in pinned host memory go up and the output comes back in chunks
-    of 8192 tokens, overlapped with the layer's kernels.  Returns (ms, h2d,
-    d2h bytes per step)."""
+    (the library's default: 16384 tokens, quarter- and half-size at both
+    ends), overlapped with the layer's kernels.  Returns (ms, h2d, d2h bytes
+    per step)."""
     import torch
 
     T, D = x.shape

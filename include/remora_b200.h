@@ -274,10 +274,12 @@ int remora_b200_moe_layer_bf16(const void* x, const void* wr, const void* wg, co
 /* The same layer with the tokens and the output in HOST memory, for callers
  * whose activations live on the host (remora's harness fills host vectors,
  * compiler/gpu_tests.cpp:48-56): the tokens go up and the output comes back
- * in chunks of chunk_tokens (0 = 8192) on two copy streams of the library's
+ * in chunks of chunk_tokens (0 = 16384) on two copy streams of the library's
  * own, overlapped with the layer's kernels on `stream` (chunk c computes
- * while chunk c+1 goes up and chunk c-1 comes down; tokens are independent,
- * so the output is bit-identical to remora_b200_moe_layer_bf16).  Weights
+ * while chunk c+1 goes up and chunk c-1 comes down; from T >= 2 chunks the
+ * first two and last two chunks are a quarter and a half of the others, so
+ * the copies nothing overlaps are short; tokens are independent, so the
+ * output is bit-identical to remora_b200_moe_layer_bf16).  Weights
  * and router are device pointers.  x_host and out_host should be pinned
  * (cudaHostAlloc / cudaHostRegister); pageable memory is correct but its
  * copies do not overlap.  The call only enqueues work: out_host is complete

@@ -436,7 +436,7 @@ int host_pipe(HostPipe** out) {
   return REMORA_B200_OK;
 }
 
-constexpr int64_t kHostChunkTokens = 8192;
+constexpr int64_t kHostChunkTokens = 16384;
 
 int64_t host_chunk(int64_t T, int64_t chunk_tokens) {
   const int64_t c = chunk_tokens > 0 ? chunk_tokens : kHostChunkTokens;
@@ -597,10 +597,27 @@ extern "C" int remora_b200_moe_layer_host_bf16(const void* x_host, const void* w
   RB_CUDA(cudaEventRecord(p->start, st));
   RB_CUDA(cudaStreamWaitEvent(p->up, p->start, 0));
   RB_CUDA(cudaStreamWaitEvent(p->down, p->start, 0));
-  const int64_t nc = (T + C - 1) / C;
-  for (int64_t c = 0; c < nc; ++c) {
-    const int b = (int)(c & 1);
-    const int64_t t0 = c * C, tc = std::min<int64_t>(C, T - t0);
+  // Chunk sizes: with T >= 2C the first two chunks are C/4 and C/2 and the last
+  // two C/2 and C/4, so the copy in of the first chunk and the copy out of the
+  // last one, which nothing overlaps, are short; the rest is split into
+  // near-equal chunks of at most C.
+  int64_t sizes[64];
+  int nc = 0;
+  const int64_t mid = T - 2 * (C / 4 + C / 2);
+  const int64_t nm = (mid + C - 1) / C;
+  if (T >= 2 * C && C >= 4 && nm <= 60) {
+    const int64_t head[2] = {C / 4, C / 2};
+    sizes[nc++] = head[0];
+    sizes[nc++] = head[1];
+    for (int64_t i = 0; i < nm; ++i) sizes[nc++] = mid / nm + (i < mid % nm ? 1 : 0);
+    sizes[nc++] = head[1];
+    sizes[nc++] = head[0];
+  }
+  int64_t t0 = 0;
+  int last = 0;
+  for (int c = 0; t0 < T; ++c) {
+    const int b = c & 1;
+    const int64_t tc = c < nc ? sizes[c] : std::min<int64_t>(C, T - t0);
     const size_t bytes = (size_t)tc * D * 2;
     if (c >= 2) RB_CUDA(cudaStreamWaitEvent(p->up, p->done[b], 0));
     RB_CUDA(cudaMemcpyAsync(xb[b], static_cast<const uint8_t*>(x_host) + (size_t)t0 * D * 2,
@@ -614,9 +631,11 @@ extern "C" int remora_b200_moe_layer_host_bf16(const void* x_host, const void* w
     RB_CUDA(cudaMemcpyAsync(static_cast<uint8_t*>(out_host) + (size_t)t0 * D * 2, ob[b], bytes,
                             cudaMemcpyDeviceToHost, p->down));
     RB_CUDA(cudaEventRecord(p->d2h[b], p->down));
+    t0 += tc;
+    last = b;
   }
   // the call is complete on `stream` once the last output chunk is down
-  RB_CUDA(cudaStreamWaitEvent(st, p->d2h[(nc - 1) & 1], 0));
+  RB_CUDA(cudaStreamWaitEvent(st, p->d2h[last], 0));
   return REMORA_B200_OK;
 }
 

@@ -154,11 +154,12 @@ def test_moe_layer_parity(rb, orc, T, D, F, E, k):
     assert norm_err(got, r) <= TOL
 
 
-@pytest.mark.parametrize("T,chunk", [(1000, 256), (777, 0), (4096, 1000)])
+@pytest.mark.parametrize("T,chunk", [(1000, 256), (777, 0), (4096, 1000), (8192, 512)])
 def test_moe_layer_host_buffers_match_device_layer(rb, orc, T, chunk):
     """Tokens and output in pinned host memory, copied in chunks (a ragged
-    last chunk; one chunk when chunk_tokens=0 covers T) overlapped with the
-    layer: bit-identical to the device-buffer layer."""
+    last chunk; one chunk when chunk_tokens=0 covers T; from T >= 4 chunks the
+    quarter- and half-size first and last chunks) overlapped with the layer:
+    bit-identical to the device-buffer layer."""
     D, F, E, k = 256, 128, 16, 4
     x, wr, wg, wu, wd = _moe_inputs(orc, T, D, F, E)
     dev = [from_np_bf16(a) for a in (x, wr, wg, wu, wd)]
