@@ -132,6 +132,8 @@ int router_launch(const void* x, const void* wr, int64_t T, int64_t D, int E, in
   if (T == 0) return REMORA_B200_OK;
   RB_CHECK_ARG(x && wr && idx && w, "router: null pointer");
   RB_CHECK_ARG(aligned16(x), "router: x must be 16-byte aligned");
+  RB_CHECK_ARG(E % 8 != 0 || aligned16(wr),
+               "router: wr must be 16-byte aligned (its rows are read 8 experts at a time)");
   RB_CHECK_ARG(T < (1ll << 31) && D < (1ll << 31), "router: sizes exceed 2^31");
   RB_CHECK_ARG(E % 8 == 0 || E <= 128, "router: E=%d must be a multiple of 8 above 128", E);
   const RouterPlan pl = router_plan(T, E);

@@ -144,3 +144,16 @@ def test_host_buffer_layer_validates_before_cuda():
     assert rc == rb.ERR_INVALID and "workspace" in rb.last_error()
     rc = L.remora_b200_moe_layer_host_bf16(p, p, p, p, p, p, 100, 256, 128, 8, 2, 0, p, 16, None)
     assert rc == rb.ERR_INVALID and "workspace" in rb.last_error()
+
+
+def test_router_rejects_unaligned_operands_before_cuda():
+    import remora_b200 as rb
+
+    L = rb.lib()
+    a = ctypes.c_void_p(4096)
+    odd = ctypes.c_void_p(4096 + 2)
+    # x and (with E % 8 == 0) the router rows are read 16 bytes at a time
+    rc = L.remora_b200_moe_router_topk_bf16(odd, a, 64, 256, 64, 8, a, a, None)
+    assert rc == rb.ERR_INVALID and "x must be 16-byte aligned" in rb.last_error()
+    rc = L.remora_b200_moe_router_topk_bf16(a, odd, 64, 256, 64, 8, a, a, None)
+    assert rc == rb.ERR_INVALID and "wr must be 16-byte aligned" in rb.last_error()
