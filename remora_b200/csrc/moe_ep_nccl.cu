@@ -338,7 +338,7 @@ extern "C" int remora_b200_moe_ep_nccl_bf16(const void* x, const void* wr, const
   if ((rc = dispatch_launch(L.idx, T, k, E, L.counts, L.offsets, L.perm, L.inv, L.block_counts,
                             st)))
     return rc;
-  if ((rc = gather_launch(x, L.perm, n, k, D, L.xs, st))) return rc;
+  if ((rc = scatter_launch(x, L.inv, T, k, D, L.xs, st))) return rc;  // rows in dispatch order
 
   // per-local-expert counts: rank q gets counts[q*Epr .. (q+1)*Epr)
   if ((r = A->GroupStart()) != ncclSuccess) return abort_fail(A, c, r, "ncclGroupStart");
