@@ -56,9 +56,9 @@ NCU_TRAFFIC_BYTES = {
     # one-rank capture of the merged expert kernel at the per-rank shape of the 8-GPU
     # layer (65536 rows): profiles/moe_ep_experts_p1_8x65536_full.md
     "moe_ep_experts": 1321200000,
-    # [2,16,4096,128] capture (155.2 MB) scaled by 4 to the [4,32,4096,128] launch:
-    # profiles/attention_causal_2x16x4096_full.md
-    "attention": 620900352,
+    # [2,16,4096,128] capture of the persistent kernel (156.1 MB) scaled by 4 to the
+    # [4,32,4096,128] launch: profiles/attention_causal_2x16x4096_full.md
+    "attention": 624540736,
 }
 
 MOE_CONFIGS = {
@@ -748,7 +748,7 @@ def bench_attention(args, world, rank, local):
     flop = 4.0 * B * H * S * S * Dh / 2.0
     peaks, src = load_peaks()
     achieved = flop / world / (ms_local * 1e-3) / 1e12
-    roof = _tensor_roofline(achieved, peaks, src, "rb::attn::k_attention_fwd",
+    roof = _tensor_roofline(achieved, peaks, src, "rb::attnp::k_attention_persist",
                             NCU_TRAFFIC_BYTES.get("attention"), kernel_ms=ms_local)
     return _line(args, world, flop / (ms * 1e-3) / 1e12, "TFLOP/s", ms, "strong", "bf16",
                  "synthetic (seeded N(0,1) bf16)", roof,

@@ -133,9 +133,10 @@ extern "C" int remora_b200_launch_plan(const char* test, const char* config, cha
     const int64_t chunks = (S + 2 * attn::BQ - 1) / (2 * attn::BQ);
     t.add("remora_b200_attention_fwd_bf16(q, k, v, out bf16[%lld,%lld,%lld,128], causal)\n", B, H,
           S);
-    t.add("  rb::attn::k_attention_fwd  grid %lld x block %d, smem %u B (one CTA per (b,h) and "
-          "256 query rows)\n",
-          (long long)(chunks * B * H), attn::kThreads, attn::kSmemBytes);
+    const long long items = (long long)(chunks * B * H);
+    t.add("  rb::attnp::k_attention_persist  grid %lld x block %d, smem %u B (persistent: %lld "
+          "work items of one (b,h) and 256 query rows)\n",
+          std::min<long long>(items, num_sms()), attnp::kThreads, attn::kSmemBytes, items);
   } else if (kind == "moe") {
     if (c.empty() || c == "4")
       moe_plan(t, 8192, 4096, 14336, 8, 2);
