@@ -58,7 +58,7 @@ NCU_TRAFFIC_BYTES = {
     "moe_ep_experts": 1321200000,
     # [2,16,4096,128] capture of the persistent kernel (156.1 MB) scaled by 4 to the
     # [4,32,4096,128] launch: profiles/attention_causal_2x16x4096_full.md
-    "attention": 624540736,
+    "attention": 624541696,
 }
 
 MOE_CONFIGS = {
